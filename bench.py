@@ -1,0 +1,360 @@
+"""Benchmark of the fused AdamW-SR step at the Llama-3-8B shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+A step is one optimizer step of the whole parameter set: 291 tensors,
+8,030,261,248 BF16 parameters with BF16 gradients ~N(0, 1e-4), FP8 E4M3
+stochastic first moment and BF16 stochastic second moment, lr 3e-4, weight
+decay 0.1, seed 7.  With N GPUs the step is sharded ZeRO-1 style (each rank
+updates its flat shard, states exist only for it) and the updated BF16
+parameters are reassembled with an in-place NCCL all-gather, which is part
+of the timed step.  Inputs are synthetic and resident in HBM (56 GB per GPU
+at N=1, far above the 126 MB L2, so no cache flush is needed).
+
+Prints one JSON line (rank 0): value = parameters updated per second by the
+whole job; roofline = the fused kernel's algorithmic HBM bytes per second
+against the measured copy bandwidth; e2e = the same step through the public
+optimizer API with the gradients copied in from pinned host memory and the
+updated parameters copied back every step; cpu_baseline = the CPU oracle on
+this host's cores over a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "stochastic-rounding-pytorch_b200"))
+
+METRIC = "AdamW-SR step params/sec & HBM GB/s (% of peak) at 8B shape, 1/2/4/8 B200"
+# Algorithmic bytes per parameter: read p, g, m, v; write p, m, v
+# (BF16 p/g = 2 B, E4M3 m = 1 B, BF16 v = 2 B): 2+2+1+2 + 2+1+2 = 12.
+BYTES_PER_PARAM = 12
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--e2e-steps", type=int, default=3)
+    parser.add_argument("--cpu-seconds", type=float, default=12.0,
+                        help="CPU work budget of the CPU baseline sample")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args(argv)
+
+
+def measured_hbm_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (copy)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
+
+
+# ------------------------------------------------------------ distributed --
+
+def init_distributed(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- clocks --
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while active."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported when NVML is usable
+            self._nvml = None
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(
+                    self._handle, self._nvml.NVML_CLOCK_SM))
+                mask = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.reasons |= {n for n, bit in self.REASONS.items() if mask & bit}
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread.is_alive():
+            self._thread.join()
+
+    def report(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# -------------------------------------------------------------- workload --
+
+def build_workload(world, rank):
+    """Flat BF16 parameter and gradient buffers holding the 291 tensors; the
+    optimizer (ZeRO-1 when world > 1) over views of them."""
+    import torch
+
+    from sr_states import StateFormat
+    from sr_states.distributed import ZeroAdamW
+    from sr_states.shapes import llama3_8b
+
+    shapes = [s for _, s in llama3_8b()]
+    total = sum(math.prod(s) for s in shapes)
+    device = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=device).manual_seed(7)
+    flat_p = torch.empty(total, dtype=torch.bfloat16, device=device).normal_(0, 0.02,
+                                                                              generator=gen)
+    flat_g = torch.empty(total, dtype=torch.bfloat16, device=device).normal_(0, 1e-4,
+                                                                              generator=gen)
+    params, offset = [], 0
+    for shape in shapes:
+        n = math.prod(shape)
+        p = torch.nn.Parameter(flat_p[offset:offset + n].view(shape))
+        p.grad = flat_g[offset:offset + n].view(shape)
+        params.append(p)
+        offset += n
+    fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn, "stochastic"),
+           "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
+    opt = ZeroAdamW(params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1,
+                    state_format=fmt, seed=7)
+    return opt, params, flat_p, flat_g, total
+
+
+def time_steps(opt, steps, world, stream):
+    """K steps bracketed by barrier + synchronize; CUDA events on the launch stream."""
+    import torch
+
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    start.record(stream)
+    for i in range(steps):
+        opt.step()
+        marks[i].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    total_ms = start.elapsed_time(end)
+    per_step = [start.elapsed_time(marks[0])] + [
+        marks[i - 1].elapsed_time(marks[i]) for i in range(1, steps)]
+    return total_ms, per_step
+
+
+def cpu_baseline(seconds):
+    """The CPU oracle (a C port of the reference algorithm) on this host's cores,
+    timed on a bounded sample of the same step: BF16 p/g, E4M3 SR m, BF16 SR v."""
+    import numpy as np
+
+    import oracle
+
+    threads = oracle.cpu_threads()
+    n = 1 << 22
+    rng = np.random.default_rng(7)
+    p = (rng.standard_normal(n, dtype=np.float32) * 0.02).view(np.uint32) >> 16
+    g = (rng.standard_normal(n, dtype=np.float32) * 1e-4).view(np.uint32) >> 16
+    p, g = p.astype(np.uint16), g.astype(np.uint16)
+    m = np.zeros(n, np.uint8)
+    v = np.zeros(n, np.uint16)
+
+    def one_pass(step):
+        oracle.adamw_(p, g, m, v, m_fmt=oracle.E4M3, m_rule=oracle.STOCHASTIC,
+                      v_fmt=oracle.BF16, v_rule=oracle.STOCHASTIC, lr=3e-4, beta1=0.9,
+                      beta2=0.999, eps=1e-8, weight_decay=0.1, step=step,
+                      update_key=oracle.update_key(7, step, 0), threads=threads)
+
+    one_pass(1)  # warm-up (page faults)
+    passes, start = 0, time.perf_counter()
+    while True:
+        one_pass(passes + 2)
+        passes += 1
+        elapsed = time.perf_counter() - start
+        if elapsed * threads >= seconds or elapsed >= seconds:
+            break
+    rate = passes * n / elapsed
+    return {"value": rate, "unit": "params/s", "cores": threads, "kind": "port",
+            "sample": f"{passes} passes over {n} elements (BF16 p/g, E4M3 SR m, BF16 SR v), "
+                      f"{elapsed:.2f} s wall on {threads} threads"}
+
+
+def e2e_run(opt, flat_p, flat_g, steps, world, total):
+    """The step through the public API with host buffers: per step the BF16
+    gradients come from pinned host memory and the updated BF16 parameters go
+    back to it (the optimizer states stay on the device)."""
+    import torch
+
+    shard = flat_g.numel()
+    host_g = torch.empty(shard, dtype=torch.bfloat16, pin_memory=True)
+    host_p = torch.empty(flat_p.numel(), dtype=torch.bfloat16, pin_memory=True)
+    host_g.copy_(flat_g)
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        flat_g.copy_(host_g, non_blocking=True)
+        opt.step()
+        host_p.copy_(flat_p, non_blocking=True)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world) / steps
+    return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": host_g.numel() * 2, "d2h_bytes_per_step": host_p.numel() * 2}
+
+
+def run_b200(args):
+    import torch
+
+    world, rank = init_distributed(args.gpus)
+    peak, peak_source = measured_hbm_peak()
+    opt, params, flat_p, flat_g, total = build_workload(world, rank)
+    local = opt.local_numel()
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    opt.timings.clear()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        total_ms, per_step = time_steps(opt, args.steps, world, stream)
+    total_ms = max_over_ranks(total_ms, world)
+    ms = total_ms / args.steps
+    kernel_ms = max_over_ranks(statistics.mean(t["update_ms"] for t in opt.timings), world)
+    gather_ms = max_over_ranks(statistics.mean(t.get("gather_ms", 0.0) for t in opt.timings),
+                               world)
+    achieved = BYTES_PER_PARAM * local / (kernel_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": total / (ms / 1e3), "unit": "params/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4)",
+                   "params": total, "tensors": len(params), "param_dtype": "bf16",
+                   "grad_dtype": "bf16", "exp_avg": "float8_e4m3fn stochastic",
+                   "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",
+                   "global_batch": None, "seq_len": None,
+                   "l2": "56 GB of inputs per step, larger than L2; no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
+                     "kernel": "srs::adamw_kernel<E4M3,BF16>", "kernel_ms": kernel_ms,
+                     "bytes_per_param": BYTES_PER_PARAM, "params_per_launch": local},
+        "allgather_ms": gather_ms if world > 1 else 0.0,
+        "step_ms_min": min(per_step), "gpu_launches": opt.launches_per_step() * args.steps,
+        "clocks": clocks.report(),
+    }
+    if not args.no_e2e:
+        line["e2e"] = e2e_run(opt, flat_p, flat_g, args.e2e_steps, world, total)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    opt.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference arm: the CPU restatement of the reference algorithm (the reference
+    itself is Python on PyTorch's CPU kernels and does not travel to this box) on all
+    host cores; every step is a bounded sample of the same workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    samples = [cpu_baseline(args.cpu_seconds / max(args.steps, 1))
+               for _ in range(args.warmup + args.steps)][args.warmup:]
+    value = statistics.median(s["value"] for s in samples)
+    base = dict(samples[-1], value=value)
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "params/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 8030261248 / value * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4), "
+                               "CPU port timed on a sample and scaled to 8,030,261,248 params",
+                   "parallelism": "host cores"},
+        "cpu_baseline": base,
+        "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

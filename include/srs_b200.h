@@ -1,0 +1,171 @@
+/*
+ * srs_b200.h — C ABI of the sm_100a stochastic-rounding optimizer library.
+ *
+ * Every entry point takes plain device addresses, element counts, POD
+ * scalars and a cudaStream_t passed as `void*`.  Nothing here allocates
+ * device memory: callers own every buffer (inputs, outputs and the row
+ * tables of the multi-tensor steps).  Work is enqueued on the given stream
+ * of the calling thread's current device; no entry point synchronises.
+ *
+ * Return value: SRS_OK (0) or a negative SRS_ERR_* code.  The text of the
+ * most recent failure on the calling thread is available from
+ * srs_last_error().  No entry point aborts the process.
+ *
+ * Counter-hash RNG contract (identical to the Python `sr_states` package):
+ *   h32(x)        x ^= x>>16; x *= 0x7FEB352D; x ^= x>>15; x *= 0x846CA68B; x ^= x>>16   (mod 2^32)
+ *   update_key    k = h32(seed_lo ^ 0x9E3779B9); k = h32(k ^ seed_hi); k = h32(k ^ step_lo);
+ *                 k = h32(k ^ step_hi); k = h32(k ^ param_index)
+ *   state_key     h32(update_key ^ state_index)
+ *   element e of a stored state uses h32((e + offset + state_key) mod 2^32);
+ *   element e of a standalone cast uses h32((e + offset + seed) mod 2^32).
+ */
+#ifndef SRS_B200_H
+#define SRS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SRS_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+#define SRS_OK 0
+#define SRS_ERR_INVALID_ARGUMENT (-1) /* bad pointer, size, format, rule or flag */
+#define SRS_ERR_UNSUPPORTED_DEVICE (-2) /* current device is not compute capability 10.0 */
+#define SRS_ERR_CUDA (-3)             /* a CUDA runtime call failed (launch, attribute query) */
+
+/* ---- storage formats (state, cast output) ------------------------------ */
+#define SRS_FMT_F32 0
+#define SRS_FMT_BF16 1
+#define SRS_FMT_F16 2
+#define SRS_FMT_E4M3 3 /* torch.float8_e4m3fn, saturating to +-448 */
+#define SRS_FMT_E5M2 4 /* torch.float8_e5m2, saturating to +-57344 */
+
+/* ---- rounding rules ---------------------------------------------------- */
+#define SRS_RULE_NEAREST 0    /* round to nearest, ties to even */
+#define SRS_RULE_STOCHASTIC 1 /* counter-hash stochastic rounding */
+
+/* ---- multi-tensor row table -------------------------------------------- */
+#define SRS_ROW_PARAM_BF16 0x1u  /* parameter is BF16 (else FP32) */
+#define SRS_ROW_GRAD_BF16 0x2u   /* gradient is BF16 (else FP32) */
+#define SRS_ROW_VECTOR_OK 0x4u   /* every base address is aligned for 8-element vector access */
+#define SRS_ROW_CLASS_SHIFT 8    /* bits 8..15: index of the row's AdamW step class */
+#define SRS_MAX_STEP_CLASSES 32
+
+/*
+ * One row = one contiguous run of `numel` elements of one parameter (a whole
+ * parameter, or its intersection with this rank's ZeRO-1 shard).  Rows are
+ * ordered by tile_begin; row i covers tiles [tile_begin_i, tile_begin_{i+1})
+ * and tile_begin_i + ceil(numel_i / srs_tile_elems()) == tile_begin_{i+1}.
+ */
+typedef struct srs_row {
+  uint64_t param;       /* device address of the parameter run (FP32 or BF16)    */
+  uint64_t grad;        /* device address of the gradient run (FP32 or BF16)     */
+  uint64_t state[2];    /* device addresses of the state runs (state[1]: AdamW)  */
+  int64_t numel;        /* > 0                                                    */
+  int64_t tile_begin;   /* first tile of this row in the launch's tile space      */
+  uint32_t param_index; /* global parameter position (low 32 bits), or the update
+                           key itself when the launch uses SRS_KEY_GIVEN          */
+  uint32_t offset;      /* flat element index of element 0 within its parameter,
+                           mod 2^32 (the shard start of the RNG contract)        */
+  uint32_t flags;       /* SRS_ROW_* bits and the step class                     */
+  uint32_t reserved;    /* zero                                                   */
+} srs_row;
+
+/* How the per-row update key is obtained. */
+#define SRS_KEY_DERIVE 0 /* update_key(seed words, step words, row.param_index) */
+#define SRS_KEY_GIVEN 1  /* row.param_index already holds the update key        */
+
+typedef struct srs_rng {
+  uint32_t seed_lo, seed_hi; /* low 64 bits of the group seed   */
+  uint32_t step_lo, step_hi; /* low 64 bits of the global RNG step */
+  int32_t key_mode;          /* SRS_KEY_DERIVE or SRS_KEY_GIVEN  */
+} srs_rng;
+
+/*
+ * AdamW scalars, each the FP32 rounding of the double-precision expression:
+ *   beta1, beta2, one_minus_beta1 = 1-beta1, one_minus_beta2 = 1-beta2,
+ *   eps, decay = 1 - lr*weight_decay,
+ *   per step class c (bias-correction step t_c):
+ *     neg_step_size[c] = -lr / (1 - beta1^t_c),  bias2_sqrt[c] = (1 - beta2^t_c)^0.5
+ * Per element (FP32, each operation rounded once):
+ *   m' = fma(g, 1-b1, m*b1);  v' = fma((1-b2)*g, g, v*b2)
+ *   d  = sqrt(v') / bias2_sqrt + eps;  p' = p*decay + (neg_step_size*m') / d
+ */
+typedef struct srs_adamw_hparams {
+  float beta1, beta2, one_minus_beta1, one_minus_beta2;
+  float eps, decay;
+  int32_t n_step_classes; /* 1..SRS_MAX_STEP_CLASSES */
+  float neg_step_size[SRS_MAX_STEP_CLASSES];
+  float bias2_sqrt[SRS_MAX_STEP_CLASSES];
+} srs_adamw_hparams;
+
+/* SGDM scalars: u' = u*momentum + g;  p' = fma(u', neg_lr, p), neg_lr = -lr. */
+typedef struct srs_sgdm_hparams {
+  float momentum;
+  float neg_lr;
+} srs_sgdm_hparams;
+
+/* ---- library information ----------------------------------------------- */
+int srs_abi_version(void);
+/* Elements per tile of the multi-tensor steps (row tile_begin arithmetic). */
+int64_t srs_tile_elems(void);
+/* Text of the last failure on this thread ("" if none). */
+const char* srs_last_error(void);
+/* SRS_OK if the current device can run the kernels (compute capability 10.0). */
+int srs_check_device(void);
+
+/* ---- standalone cast ---------------------------------------------------
+ * Replaces sr_states/triton/cast.py:32-60 (`cast`) and
+ * sr_states/triton/sr_cast.py:89-128 (`sr_cast_bf16`, `rn_cast_bf16`).
+ * y[e] = round(x[e]) into `out_format` under `rule`; the stochastic counter of
+ * element e is (e + offset + seed) mod 2^32.  SRS_FMT_F32 copies.  x and y must
+ * not overlap.  n == 0 is a no-op.
+ */
+int srs_cast(const float* x, void* y, int64_t n, int out_format, int rule, uint32_t seed,
+             uint32_t offset, int grid_ctas, void* stream);
+
+/* ---- fused multi-tensor steps -------------------------------------------
+ * Replace the per-bucket launches of sr_states/triton/adamw.py:303-317
+ * (_multi_adamw_kernel) and sr_states/triton/sgd.py:542-556
+ * (_multi_sgdm_kernel): ONE launch covers every row of a parameter group on
+ * one device, whatever the rows' parameter/gradient dtypes and AdamW
+ * bias-correction steps.  `rows` is a device array of n_rows srs_row;
+ * n_tiles = tile_begin of the last row + its tile count.  grid_ctas <= 0
+ * selects the persistent grid (a multiple of the SM count).
+ */
+int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
+                    int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
+                    const srs_rng* rng, int grid_ctas, void* stream);
+
+int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
+                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng, int grid_ctas,
+                   void* stream);
+
+/* ---- fused single-tensor steps ------------------------------------------
+ * Replace sr_states/triton/adamw.py:160-221 (`triton_adamw_step_`) and
+ * sr_states/triton/sgd.py:115-171 (`triton_sgdm_step_`).  `row` is a HOST
+ * srs_row describing one tensor; its param_index field holds the update key
+ * (the functional API's `seed`).  hp->n_step_classes must be 1.
+ */
+int srs_adamw_single(const srs_row* row, int m_format, int m_rule, int v_format, int v_rule,
+                     const srs_adamw_hparams* hp, int grid_ctas, void* stream);
+
+int srs_sgdm_single(const srs_row* row, int u_format, int u_rule, const srs_sgdm_hparams* hp,
+                    int grid_ctas, void* stream);
+
+/* ---- RNG key derivation on the device ----------------------------------
+ * Mirrors sr_states/triton/_keys.py:20-30 (_update_key/_state_key), used to
+ * check that device keys equal host keys.  For each i < n writes
+ * out[3i..3i+2] = {update_key(words, param_index[i]), state_key(k, 0), state_key(k, 1)}.
+ */
+int srs_derive_keys(const uint32_t* param_index, uint32_t* out, int64_t n, const srs_rng* rng,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SRS_B200_H */

@@ -1,0 +1,305 @@
+// extern "C" entry points of libsrs_b200.so (declared in include/srs_b200.h):
+// argument validation, device capability check, persistent-grid sizing and
+// dispatch from runtime formats to the kernel instantiations.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <unordered_map>
+
+#include "srs_kernels.cuh"
+
+namespace srs {
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SRS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+constexpr int kMaxDevices = 128;
+std::mutex g_mutex;
+int g_device_ok[kMaxDevices];  // 0 unknown, 1 usable, -1 unusable
+int g_sm_count[kMaxDevices];
+std::unordered_map<const void*, int> g_blocks_per_sm[kMaxDevices];
+
+int current_device(int* dev) {
+  const cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(SRS_ERR_UNSUPPORTED_DEVICE, "device %d", *dev);
+  return SRS_OK;
+}
+
+int check_device() {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_device_ok[dev] == 0) {
+    int major = 0, minor = 0, sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    g_sm_count[dev] = sms;
+    g_device_ok[dev] = (major == 10 && minor == 0) ? 1 : -1;
+    if (g_device_ok[dev] < 0) {
+      return fail(SRS_ERR_UNSUPPORTED_DEVICE,
+                  "device %d has compute capability %d.%d; these kernels are built for sm_100a "
+                  "(compute capability 10.0, B200)",
+                  dev, major, minor);
+    }
+  } else if (g_device_ok[dev] < 0) {
+    return fail(SRS_ERR_UNSUPPORTED_DEVICE,
+                "device %d is not compute capability 10.0 (sm_100a kernels)", dev);
+  }
+  return SRS_OK;
+}
+
+bool valid_format(int f) { return f >= SRS_FMT_F32 && f <= SRS_FMT_E5M2; }
+bool valid_rule(int r) { return r == SRS_RULE_NEAREST || r == SRS_RULE_STOCHASTIC; }
+
+int check_hp_classes(int n) {
+  if (n < 1 || n > SRS_MAX_STEP_CLASSES)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "n_step_classes must be in [1, %d], got %d",
+                SRS_MAX_STEP_CLASSES, n);
+  return SRS_OK;
+}
+
+using AdamWLaunch = cudaError_t (*)(const srs_row*, int64_t, int64_t, const AdamWArgs&, int,
+                                    cudaStream_t);
+using SgdmLaunch = cudaError_t (*)(const srs_row*, int64_t, int64_t, const SgdmArgs&, int,
+                                   cudaStream_t);
+using CastLaunch = cudaError_t (*)(const float*, void*, int64_t, uint32_t, int, int, int,
+                                   cudaStream_t);
+
+#define SRS_ROW5(M)                                                                     \
+  {&launch_adamw<M, 0>, &launch_adamw<M, 1>, &launch_adamw<M, 2>, &launch_adamw<M, 3>, \
+   &launch_adamw<M, 4>}
+const AdamWLaunch kAdamW[5][5] = {SRS_ROW5(0), SRS_ROW5(1), SRS_ROW5(2), SRS_ROW5(3),
+                                  SRS_ROW5(4)};
+#undef SRS_ROW5
+const SgdmLaunch kSgdm[5] = {&launch_sgdm<0>, &launch_sgdm<1>, &launch_sgdm<2>, &launch_sgdm<3>,
+                             &launch_sgdm<4>};
+const CastLaunch kCast[5] = {&launch_cast<0>, &launch_cast<1>, &launch_cast<2>, &launch_cast<3>,
+                             &launch_cast<4>};
+
+int fmt_bytes(int f) { return f == SRS_FMT_F32 ? 4 : (f <= SRS_FMT_F16 ? 2 : 1); }
+
+__global__ void derive_keys_kernel(const uint32_t* __restrict__ index, uint32_t* __restrict__ out,
+                                   int64_t n, const srs_rng rng) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const uint32_t k = update_key(rng, index[i]);
+    out[3 * i] = k;
+    out[3 * i + 1] = state_key(k, 0u);
+    out[3 * i + 2] = state_key(k, 1u);
+  }
+}
+
+}  // namespace
+
+int grid_for(const void* kernel, int64_t work_ctas, int grid_ctas, cudaError_t* err) {
+  *err = cudaSuccess;
+  if (work_ctas <= 0) return 1;
+  if (grid_ctas > 0) return (int)(work_ctas < grid_ctas ? work_ctas : grid_ctas);
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return 0;
+  int per_sm = 0, sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    sms = g_sm_count[dev];
+    auto it = g_blocks_per_sm[dev].find(kernel);
+    if (it != g_blocks_per_sm[dev].end()) per_sm = it->second;
+  }
+  if (per_sm == 0) {
+    *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
+    if (*err != cudaSuccess) return 0;
+    if (per_sm < 1) per_sm = 1;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    g_blocks_per_sm[dev][kernel] = per_sm;
+  }
+  if (sms <= 0) sms = 148;
+  const int64_t full = (int64_t)sms * per_sm;
+  return (int)(work_ctas < full ? work_ctas : full);
+}
+
+}  // namespace srs
+
+using namespace srs;
+
+extern "C" {
+
+int srs_abi_version(void) { return SRS_ABI_VERSION; }
+
+int64_t srs_tile_elems(void) { return kTile; }
+
+const char* srs_last_error(void) { return g_error; }
+
+int srs_check_device(void) {
+  g_error[0] = '\0';
+  return check_device();
+}
+
+int srs_cast(const float* x, void* y, int64_t n, int out_format, int rule, uint32_t seed,
+             uint32_t offset, int grid_ctas, void* stream) {
+  g_error[0] = '\0';
+  if (n < 0) return fail(SRS_ERR_INVALID_ARGUMENT, "n must be non-negative, got %lld", (long long)n);
+  if (!valid_format(out_format))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown output format %d", out_format);
+  if (!valid_rule(rule)) return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule %d", rule);
+  if (n == 0) return SRS_OK;
+  if (x == nullptr || y == nullptr)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null input or output pointer");
+  if (int rc = check_device()) return rc;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(x), ya = reinterpret_cast<uintptr_t>(y);
+  const int yb = fmt_bytes(out_format);
+  if (xa % 4 != 0 || ya % yb != 0)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "input/output pointers are not element aligned");
+  const int ya_need = yb * kVec < 16 ? yb * kVec : 16;
+  const int vec_ok = (xa % 16 == 0) && (ya % ya_need == 0);
+  const cudaError_t e = kCast[out_format](x, y, n, seed + offset, rule, vec_ok, grid_ctas,
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_cast launch");
+}
+
+static int check_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, const void* hp,
+                       const srs_rng* rng) {
+  if (hp == nullptr || rng == nullptr)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null hyperparameter or rng pointer");
+  if (rng->key_mode != SRS_KEY_DERIVE && rng->key_mode != SRS_KEY_GIVEN)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown key_mode %d", rng->key_mode);
+  if (n_rows < 0 || n_tiles < 0) return fail(SRS_ERR_INVALID_ARGUMENT, "negative row/tile count");
+  if (n_tiles > 0 && (rows == nullptr || n_rows == 0))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "tiles given without rows");
+  if (reinterpret_cast<uintptr_t>(rows) % 16 != 0)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "row table must be 16-byte aligned");
+  return SRS_OK;
+}
+
+int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
+                    int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
+                    const srs_rng* rng, int grid_ctas, void* stream) {
+  g_error[0] = '\0';
+  if (!valid_format(m_format) || !valid_format(v_format))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format (%d, %d)", m_format, v_format);
+  if (!valid_rule(m_rule) || !valid_rule(v_rule))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule (%d, %d)", m_rule, v_rule);
+  if (int rc = check_multi(rows, n_rows, n_tiles, hp, rng)) return rc;
+  if (int rc = check_hp_classes(hp->n_step_classes)) return rc;
+  if (n_tiles == 0) return SRS_OK;
+  if (int rc = check_device()) return rc;
+  AdamWArgs a{};
+  a.hp = *hp;
+  a.rng = *rng;
+  a.m_stochastic = m_rule;
+  a.v_stochastic = v_rule;
+  const cudaError_t e = kAdamW[m_format][v_format](rows, n_rows, n_tiles, a, grid_ctas,
+                                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_multi launch");
+}
+
+int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
+                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng, int grid_ctas,
+                   void* stream) {
+  g_error[0] = '\0';
+  if (!valid_format(u_format))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format %d", u_format);
+  if (!valid_rule(u_rule)) return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule %d", u_rule);
+  if (int rc = check_multi(rows, n_rows, n_tiles, hp, rng)) return rc;
+  if (n_tiles == 0) return SRS_OK;
+  if (int rc = check_device()) return rc;
+  SgdmArgs a{};
+  a.hp = *hp;
+  a.rng = *rng;
+  a.u_stochastic = u_rule;
+  const cudaError_t e =
+      kSgdm[u_format](rows, n_rows, n_tiles, a, grid_ctas, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_sgdm_multi launch");
+}
+
+static int check_single_row(const srs_row* row, int64_t* n_tiles) {
+  if (row == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null row");
+  if (row->numel < 0) return fail(SRS_ERR_INVALID_ARGUMENT, "negative numel");
+  *n_tiles = (row->numel + kTile - 1) / kTile;
+  if (*n_tiles > 0 && (row->param == 0 || row->grad == 0))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null parameter or gradient address");
+  return SRS_OK;
+}
+
+int srs_adamw_single(const srs_row* row, int m_format, int m_rule, int v_format, int v_rule,
+                     const srs_adamw_hparams* hp, int grid_ctas, void* stream) {
+  g_error[0] = '\0';
+  if (!valid_format(m_format) || !valid_format(v_format))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format (%d, %d)", m_format, v_format);
+  if (!valid_rule(m_rule) || !valid_rule(v_rule))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule (%d, %d)", m_rule, v_rule);
+  if (hp == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null hyperparameter pointer");
+  if (hp->n_step_classes != 1)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "a single-tensor step has exactly one step class");
+  int64_t n_tiles = 0;
+  if (int rc = check_single_row(row, &n_tiles)) return rc;
+  if (n_tiles == 0) return SRS_OK;
+  if (row->state[0] == 0 || row->state[1] == 0)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null state address");
+  if (int rc = check_device()) return rc;
+  AdamWArgs a{};
+  a.inline_row = *row;
+  a.inline_row.tile_begin = 0;
+  a.inline_row.flags &= ~(0xFFu << SRS_ROW_CLASS_SHIFT);
+  a.hp = *hp;
+  a.rng.key_mode = SRS_KEY_GIVEN;
+  a.m_stochastic = m_rule;
+  a.v_stochastic = v_rule;
+  const cudaError_t e = kAdamW[m_format][v_format](nullptr, 1, n_tiles, a, grid_ctas,
+                                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_single launch");
+}
+
+int srs_sgdm_single(const srs_row* row, int u_format, int u_rule, const srs_sgdm_hparams* hp,
+                    int grid_ctas, void* stream) {
+  g_error[0] = '\0';
+  if (!valid_format(u_format))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format %d", u_format);
+  if (!valid_rule(u_rule)) return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule %d", u_rule);
+  if (hp == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null hyperparameter pointer");
+  int64_t n_tiles = 0;
+  if (int rc = check_single_row(row, &n_tiles)) return rc;
+  if (n_tiles == 0) return SRS_OK;
+  if (row->state[0] == 0) return fail(SRS_ERR_INVALID_ARGUMENT, "null state address");
+  if (int rc = check_device()) return rc;
+  SgdmArgs a{};
+  a.inline_row = *row;
+  a.inline_row.tile_begin = 0;
+  a.hp = *hp;
+  a.rng.key_mode = SRS_KEY_GIVEN;
+  a.u_stochastic = u_rule;
+  const cudaError_t e =
+      kSgdm[u_format](nullptr, 1, n_tiles, a, grid_ctas, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_sgdm_single launch");
+}
+
+int srs_derive_keys(const uint32_t* param_index, uint32_t* out, int64_t n, const srs_rng* rng,
+                    void* stream) {
+  g_error[0] = '\0';
+  if (n < 0 || rng == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (n == 0) return SRS_OK;
+  if (param_index == nullptr || out == nullptr)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = check_device()) return rc;
+  const int blocks = (int)((n + 255) / 256);
+  derive_keys_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(param_index, out, n,
+                                                                             *rng);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_derive_keys launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,32 @@
+// AdamW step kernels for one first-moment format (SRS_M_FORMAT, set by the
+// build: one object per format) and every second-moment format.
+#include "srs_kernels.cuh"
+
+#ifndef SRS_M_FORMAT
+#error "compile once per first-moment format with -DSRS_M_FORMAT=<0..4>"
+#endif
+
+namespace srs {
+
+template <int MF, int VF>
+cudaError_t launch_adamw(const srs_row* rows, int64_t n_rows, int64_t n_tiles,
+                         const AdamWArgs& a, int grid_ctas, cudaStream_t stream) {
+  cudaError_t err = cudaSuccess;
+  const int grid = grid_for(reinterpret_cast<const void*>(&adamw_kernel<MF, VF>), n_tiles,
+                            grid_ctas, &err);
+  if (err != cudaSuccess) return err;
+  adamw_kernel<MF, VF><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
+  return cudaGetLastError();
+}
+
+#define SRS_INSTANTIATE(VF)                                                               \
+  template cudaError_t launch_adamw<SRS_M_FORMAT, VF>(const srs_row*, int64_t, int64_t, \
+                                                      const AdamWArgs&, int, cudaStream_t);
+SRS_INSTANTIATE(SRS_FMT_F32)
+SRS_INSTANTIATE(SRS_FMT_BF16)
+SRS_INSTANTIATE(SRS_FMT_F16)
+SRS_INSTANTIATE(SRS_FMT_E4M3)
+SRS_INSTANTIATE(SRS_FMT_E5M2)
+#undef SRS_INSTANTIATE
+
+}  // namespace srs

@@ -1,0 +1,378 @@
+// Device-side building blocks shared by every sm_100a kernel of the library:
+// the counter hash and key derivation, FP32/BF16/FP16/FP8 loads and stores of
+// 8-element vectors, and the nearest / stochastic storage rounding rules.
+//
+// Numerical contract (bit-exact with the reference CPU implementation):
+//   hash            sr_states/_hash.py:10-15 and :31-50
+//   keys            sr_states/_hash.py:18-28, device mirror sr_states/triton/_keys.py:20-30
+//   BF16 stochastic sr_states/_bf16.py:37-74
+//   FP16/FP8 rules  sr_states/_minifloat.py:10-70 (24-bit probability grid, saturating FP8)
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include "srs_b200.h"
+
+namespace srs {
+
+constexpr int kThreads = 256;              // CTA size of every kernel
+constexpr int kVec = 8;                    // elements per thread per tile
+constexpr int64_t kTile = kThreads * kVec; // elements per tile (row table unit)
+
+// ---------------------------------------------------------------- hashing --
+
+__device__ __forceinline__ uint32_t h32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7FEB352Du;
+  x ^= x >> 15;
+  x *= 0x846CA68Bu;
+  return x ^ (x >> 16);
+}
+
+__device__ __forceinline__ uint32_t update_key(const srs_rng& r, uint32_t param_index) {
+  uint32_t k = h32(r.seed_lo ^ 0x9E3779B9u);
+  k = h32(k ^ r.seed_hi);
+  k = h32(k ^ r.step_lo);
+  k = h32(k ^ r.step_hi);
+  return h32(k ^ param_index);
+}
+
+__device__ __forceinline__ uint32_t state_key(uint32_t key, uint32_t index) {
+  return h32(key ^ index);
+}
+
+// ------------------------------------------------------------ FP8 helpers --
+
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t pair) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)pair, __NV_E4M3);
+  return __half22float2(*reinterpret_cast<__half2*>(&h));
+}
+
+// An E5M2 byte is the high byte of the FP16 with the same value.
+__device__ __forceinline__ float2 e5m2x2_to_float2(uint32_t pair) {
+  const uint32_t w = __byte_perm(pair, 0u, 0x1404u);  // [0, b0, 0, b1]
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+__device__ __forceinline__ float2 f16x2_to_float2(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// --------------------------------------------------- stochastic rounding --
+
+// BF16: add the low 16 hash bits to the FP32 encoding and truncate.  Infinities
+// survive the addition unchanged; NaN is stored as 0xFFFF, the encoding the
+// reference's CPU conversion produces for every NaN.
+__device__ __forceinline__ uint32_t bf16_stochastic(float x, uint32_t h) {
+  const uint32_t r = (__float_as_uint(x) + (h & 0xFFFFu)) >> 16;
+  return (x != x) ? 0xFFFFu : r;
+}
+
+// Stochastic rounding of a finite, non-negative FP32 encoding `u` onto a
+// minifloat grid with M mantissa bits whose smallest normal power of two has
+// FP32 biased exponent EBMIN.  Returns the target magnitude encoding.
+//
+// The reference evaluates, in exact FP32 arithmetic,
+//   e' = max(e, emin); s = |x| * 2^(M-e'); q = floor(s);
+//   R = floor((s - q) * 2^24); up = (hash >> 8) < R; result = (q + up) * 2^(e'-M).
+// Here the same quantities are taken from the integer encoding: with the
+// significand F (implicit bit set) and d = e' - e extra shift bits,
+//   q0 = F >> (23-M), r0 = F << (9+M) (the 23-M discarded bits, left-aligned),
+//   q = q0 >> d, and floor((s-q) * 2^32) = low word of (q0:r0) >> d.
+// Clearing its low 8 bits turns the 32-bit fraction into R * 2^8, so
+// (hash >> 8) < R  <=>  hash < (R << 8).  Result encoding = (max(E-EBMIN,0) << M) + q + up,
+// which also carries into the next binade (or from subnormal into normal).
+// FP32 subnormals (E == 0) get a spurious implicit bit, but then d >= EBMIN - 1
+// and every retained bit is shifted out, exactly as the reference's result.
+template <int M, int EBMIN>
+__device__ __forceinline__ uint32_t grid_stochastic_magnitude(uint32_t u, uint32_t h) {
+  const int E = (int)(u >> 23);
+  const int ex = max(E - EBMIN, 0);
+  const int d = ex - E + EBMIN;  // max(EBMIN - E, 0)
+  const uint32_t q0 = ((u >> (23 - M)) & ((1u << M) - 1u)) | (1u << M);
+  const uint32_t r0 = u << (9 + M);
+  const uint32_t q = __funnelshift_rc(q0, 0u, (uint32_t)d);
+  uint32_t frac32;
+  if constexpr (M < 8) {
+    // q0 < 256: for d >= 32 the clamped shift leaves q0 >> 0 < 256, which the
+    // mask below clears, matching the exact (zero) 24-bit threshold.
+    frac32 = __funnelshift_rc(r0, q0, (uint32_t)d);
+  } else {
+    frac32 = (d < 32) ? __funnelshift_rc(r0, q0, (uint32_t)d)
+                      : __funnelshift_rc(q0, 0u, (uint32_t)(d - 32));
+  }
+  const uint32_t up = (h < (frac32 & 0xFFFFFF00u)) ? 1u : 0u;
+  return ((uint32_t)ex << M) + q + up;
+}
+
+// FP8 E4M3 (torch.float8_e4m3fn): |x| clamped to 448 first, NaN -> sign|0x7F.
+__device__ __forceinline__ uint32_t e4m3_stochastic(float x, uint32_t h) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t u = min(b & 0x7FFFFFFFu, 0x43E00000u);  // 448.0f
+  uint32_t r = grid_stochastic_magnitude<3, 121>(u, h);
+  r = (x != x) ? 0x7Fu : r;
+  return r | ((b >> 24) & 0x80u);
+}
+
+// FP8 E5M2: |x| clamped to 57344 first, NaN -> sign|0x7F.
+__device__ __forceinline__ uint32_t e5m2_stochastic(float x, uint32_t h) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t u = min(b & 0x7FFFFFFFu, 0x47600000u);  // 57344.0f
+  uint32_t r = grid_stochastic_magnitude<2, 113>(u, h);
+  r = (x != x) ? 0x7Fu : r;
+  return r | ((b >> 24) & 0x80u);
+}
+
+// FP16: IEEE behaviour.  Finite results at or above 2^16 are infinity; +-Inf
+// stays infinite; NaN keeps the F16C encoding (quiet bit, top payload bits).
+__device__ __forceinline__ uint32_t f16_stochastic(float x, uint32_t h) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t u = b & 0x7FFFFFFFu;
+  uint32_t r = min(grid_stochastic_magnitude<10, 113>(u, h), 0x7C00u);
+  if (u >= 0x7F800000u) r = (u == 0x7F800000u) ? 0x7C00u : (0x7E00u | ((u >> 13) & 0x3FFu));
+  return r | ((b >> 16) & 0x8000u);
+}
+
+// ------------------------------------------------- 8-element vector types --
+
+// Storage traits: bytes per element and 32-bit words per 8-element vector.
+template <int F> struct Fmt;
+template <> struct Fmt<SRS_FMT_F32> { static constexpr int kBytes = 4; };
+template <> struct Fmt<SRS_FMT_BF16> { static constexpr int kBytes = 2; };
+template <> struct Fmt<SRS_FMT_F16> { static constexpr int kBytes = 2; };
+template <> struct Fmt<SRS_FMT_E4M3> { static constexpr int kBytes = 1; };
+template <> struct Fmt<SRS_FMT_E5M2> { static constexpr int kBytes = 1; };
+
+template <int F> constexpr int kWords = kVec * Fmt<F>::kBytes / 4;
+
+// Raw 8-element load (16-byte aligned for 2- and 4-byte formats, 8-byte for FP8).
+template <int F>
+__device__ __forceinline__ void load_raw8(const void* base, int64_t e0, uint32_t (&w)[kWords<F>]) {
+  const char* p = static_cast<const char*>(base) + e0 * Fmt<F>::kBytes;
+  if constexpr (kWords<F> == 8) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
+    const uint4 b = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+  } else if constexpr (kWords<F> == 4) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  } else {
+    const uint2 a = __ldcs(reinterpret_cast<const uint2*>(p));
+    w[0] = a.x; w[1] = a.y;
+  }
+}
+
+template <int F>
+__device__ __forceinline__ void store_raw8(void* base, int64_t e0, const uint32_t (&w)[kWords<F>]) {
+  char* p = static_cast<char*>(base) + e0 * Fmt<F>::kBytes;
+  if constexpr (kWords<F> == 8) {
+    __stcs(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
+    __stcs(reinterpret_cast<uint4*>(p) + 1, make_uint4(w[4], w[5], w[6], w[7]));
+  } else if constexpr (kWords<F> == 4) {
+    __stcs(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
+  } else {
+    __stcs(reinterpret_cast<uint2*>(p), make_uint2(w[0], w[1]));
+  }
+}
+
+// Element j of a packed vector.
+template <int F>
+__device__ __forceinline__ uint32_t raw_element(const uint32_t (&w)[kWords<F>], int j) {
+  if constexpr (Fmt<F>::kBytes == 4) return w[j];
+  else if constexpr (Fmt<F>::kBytes == 2) return (w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+  else return (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+}
+
+// Guarded scalar load of `count` (< 8 or unaligned) elements into packed words.
+template <int F>
+__device__ __forceinline__ void load_raw_partial(const void* base, int64_t e0, int count,
+                                                 uint32_t (&w)[kWords<F>]) {
+#pragma unroll
+  for (int i = 0; i < kWords<F>; ++i) w[i] = 0u;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    if (j < count) {
+      uint32_t v;
+      if constexpr (Fmt<F>::kBytes == 4) v = static_cast<const uint32_t*>(base)[e0 + j];
+      else if constexpr (Fmt<F>::kBytes == 2) v = static_cast<const uint16_t*>(base)[e0 + j];
+      else v = static_cast<const uint8_t*>(base)[e0 + j];
+      if constexpr (Fmt<F>::kBytes == 4) w[j] = v;
+      else if constexpr (Fmt<F>::kBytes == 2) w[j >> 1] |= v << (16 * (j & 1));
+      else w[j >> 2] |= v << (8 * (j & 3));
+    }
+  }
+}
+
+template <int F>
+__device__ __forceinline__ void store_raw_partial(void* base, int64_t e0, int count,
+                                                  const uint32_t (&w)[kWords<F>]) {
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    if (j < count) {
+      const uint32_t v = raw_element<F>(w, j);
+      if constexpr (Fmt<F>::kBytes == 4) static_cast<uint32_t*>(base)[e0 + j] = v;
+      else if constexpr (Fmt<F>::kBytes == 2) static_cast<uint16_t*>(base)[e0 + j] = (uint16_t)v;
+      else static_cast<uint8_t*>(base)[e0 + j] = (uint8_t)v;
+    }
+  }
+}
+
+// Decode 8 stored elements to FP32 (exact for every format).
+template <int F>
+__device__ __forceinline__ void decode8(const uint32_t (&w)[kWords<F>], float (&x)[kVec]) {
+  if constexpr (F == SRS_FMT_F32) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) x[j] = __uint_as_float(w[j]);
+  } else if constexpr (F == SRS_FMT_BF16 || F == SRS_FMT_F16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = (F == SRS_FMT_BF16) ? bf16x2_to_float2(w[i]) : f16x2_to_float2(w[i]);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint32_t pair = (w[i] >> (16 * k)) & 0xFFFFu;
+        const float2 f = (F == SRS_FMT_E4M3) ? e4m3x2_to_float2(pair) : e5m2x2_to_float2(pair);
+        x[4 * i + 2 * k] = f.x;
+        x[4 * i + 2 * k + 1] = f.y;
+      }
+    }
+  }
+}
+
+// Round 8 FP32 values into storage format F.  Element j of a stochastic rule
+// uses the hash of counter `ctr0 + j` (mod 2^32).  FP32 storage is the identity.
+template <int F>
+__device__ __forceinline__ void encode8(const float (&x)[kVec], uint32_t ctr0, bool stochastic,
+                                        uint32_t (&w)[kWords<F>]) {
+  if constexpr (F == SRS_FMT_F32) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) w[j] = __float_as_uint(x[j]);
+  } else if constexpr (F == SRS_FMT_BF16 || F == SRS_FMT_F16) {
+    if (stochastic) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t h0 = h32(ctr0 + 2 * i), h1 = h32(ctr0 + 2 * i + 1);
+        uint32_t lo, hi;
+        if constexpr (F == SRS_FMT_BF16) {
+          lo = bf16_stochastic(x[2 * i], h0);
+          hi = bf16_stochastic(x[2 * i + 1], h1);
+        } else {
+          lo = f16_stochastic(x[2 * i], h0);
+          hi = f16_stochastic(x[2 * i + 1], h1);
+        }
+        w[i] = lo | (hi << 16);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = make_float2(x[2 * i], x[2 * i + 1]);
+        if constexpr (F == SRS_FMT_BF16) {
+          const __nv_bfloat162 b = __float22bfloat162_rn(f);
+          w[i] = *reinterpret_cast<const uint32_t*>(&b);
+        } else {
+          const __half2 hh = __float22half2_rn(f);
+          w[i] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+      }
+    }
+  } else {
+    if (stochastic) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint32_t word = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t h = h32(ctr0 + 4 * i + k);
+          const uint32_t b = (F == SRS_FMT_E4M3) ? e4m3_stochastic(x[4 * i + k], h)
+                                                 : e5m2_stochastic(x[4 * i + k], h);
+          word |= b << (8 * k);
+        }
+        w[i] = word;
+      }
+    } else {
+      // Saturating round-to-nearest-even conversion; equal to the reference's
+      // clamp-then-grid rounding (verified exhaustively against the CPU oracle).
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i], x[4 * i + 1]),
+                                                     __NV_SATFINITE,
+                                                     F == SRS_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i + 2], x[4 * i + 3]),
+                                                     __NV_SATFINITE,
+                                                     F == SRS_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
+        w[i] = (lo & 0xFFFFu) | (hi << 16);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------ parameter dtypes --
+
+// Parameters and gradients are FP32 (P_BF16 == false) or BF16.
+template <bool BF16>
+__device__ __forceinline__ void load_param8(const void* base, int64_t e0, int count, bool vec,
+                                            float (&x)[kVec]) {
+  if constexpr (BF16) {
+    uint32_t w[4];
+    if (vec) load_raw8<SRS_FMT_BF16>(base, e0, w);
+    else load_raw_partial<SRS_FMT_BF16>(base, e0, count, w);
+    decode8<SRS_FMT_BF16>(w, x);
+  } else {
+    uint32_t w[8];
+    if (vec) load_raw8<SRS_FMT_F32>(base, e0, w);
+    else load_raw_partial<SRS_FMT_F32>(base, e0, count, w);
+    decode8<SRS_FMT_F32>(w, x);
+  }
+}
+
+// Parameter write-back: FP32 as is, BF16 round-to-nearest-even.
+template <bool BF16>
+__device__ __forceinline__ void store_param8(void* base, int64_t e0, int count, bool vec,
+                                             const float (&x)[kVec]) {
+  if constexpr (BF16) {
+    uint32_t w[4];
+    encode8<SRS_FMT_BF16>(x, 0u, false, w);
+    if (vec) store_raw8<SRS_FMT_BF16>(base, e0, w);
+    else store_raw_partial<SRS_FMT_BF16>(base, e0, count, w);
+  } else {
+    uint32_t w[8];
+    encode8<SRS_FMT_F32>(x, 0u, false, w);
+    if (vec) store_raw8<SRS_FMT_F32>(base, e0, w);
+    else store_raw_partial<SRS_FMT_F32>(base, e0, count, w);
+  }
+}
+
+template <int F>
+__device__ __forceinline__ void load_state8(const void* base, int64_t e0, int count, bool vec,
+                                            float (&x)[kVec]) {
+  uint32_t w[kWords<F>];
+  if (vec) load_raw8<F>(base, e0, w);
+  else load_raw_partial<F>(base, e0, count, w);
+  decode8<F>(w, x);
+}
+
+template <int F>
+__device__ __forceinline__ void store_state8(void* base, int64_t e0, int count, bool vec,
+                                             const float (&x)[kVec], uint32_t ctr0,
+                                             bool stochastic) {
+  uint32_t w[kWords<F>];
+  encode8<F>(x, ctr0, stochastic, w);
+  if (vec) store_raw8<F>(base, e0, w);
+  else store_raw_partial<F>(base, e0, count, w);
+}
+
+}  // namespace srs

@@ -1,0 +1,206 @@
+"""ZeRO-1 sharding of the fused optimizer steps across the GPUs of one node.
+
+The parameters of all groups, in order, are laid out in one flat buffer per
+dtype, padded so that it splits into ``world`` equal shards of a multiple of
+64 elements.  Rank r updates only the elements of shard r: every intersection
+of the shard with a parameter becomes one row of the fused step, with the
+parameter's global index and, as RNG offset, the index of the row's first
+element within that parameter.  The counter-hash RNG therefore gives exactly
+the bytes of an unsharded step, whatever the world size.  Optimizer states
+exist only for the local shard.  After the update each flat buffer is
+reassembled with one in-place NCCL all-gather over NVLink.
+
+Gradients must be complete on every rank (already all-reduced), as in ZeRO-1.
+``state_dict()`` holds each rank's shard of the states.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .optim._state import _validate_rng_numel
+from .optim.adamw import AdamWReferenceSR
+from .optim.sgd import SGDMReferenceSR
+
+SHARD_ALIGN = 64  # elements; keeps every shard boundary 16-byte aligned for 2/4-byte dtypes
+
+
+class _Piece:
+    """A rank's contiguous run of one parameter, presented to the fused step like
+    a parameter: the 1-D view of the run plus the matching gradient run."""
+
+    __slots__ = ("tensor", "grad")
+
+    def __init__(self, tensor, grad):
+        self.tensor = tensor
+        self.grad = grad
+
+    def __getattr__(self, name):
+        return getattr(self.tensor, name)
+
+
+class FlatLayout:
+    """Where every parameter lives in its dtype's flat buffer and which run is local."""
+
+    def __init__(self, params, world: int, rank: int):
+        self.world, self.rank = world, rank
+        self.buffers: dict[torch.dtype, torch.Tensor] = {}
+        self.place: dict[int, tuple[torch.dtype, int]] = {}  # id(param) -> (dtype, flat offset)
+        by_dtype: dict[torch.dtype, list] = {}
+        for p in params:
+            by_dtype.setdefault(p.dtype, []).append(p)
+        for dtype, plist in by_dtype.items():
+            total = sum(p.numel() for p in plist)
+            unit = world * SHARD_ALIGN
+            padded = -(-total // unit) * unit
+            buffer = self._adopt(plist, padded)
+            if buffer is None:
+                buffer = torch.zeros(padded, dtype=dtype, device=plist[0].device)
+                offset = 0
+                for p in plist:
+                    n = p.numel()
+                    buffer[offset:offset + n].copy_(p.detach().reshape(-1))
+                    p.data = buffer[offset:offset + n].view(p.shape)
+                    offset += n
+            offset = 0
+            for p in plist:
+                self.place[id(p)] = (dtype, offset)
+                offset += p.numel()
+            self.buffers[dtype] = buffer
+
+    @staticmethod
+    def _adopt(plist, padded):
+        """The existing storage, if the parameters already sit back to back from
+        its start and it is long enough for the padded layout."""
+        storage = plist[0].untyped_storage()
+        offset = 0
+        for p in plist:
+            if (p.untyped_storage().data_ptr() != storage.data_ptr() or not p.is_contiguous()
+                    or p.storage_offset() != offset):
+                return None
+            offset += p.numel()
+        if storage.nbytes() < padded * plist[0].element_size():
+            return None
+        base = torch.empty(0, dtype=plist[0].dtype, device=plist[0].device).set_(
+            storage, 0, (padded,), (1,))
+        return base
+
+    def shard(self, dtype) -> tuple[int, int]:
+        size = self.buffers[dtype].numel() // self.world
+        return self.rank * size, (self.rank + 1) * size
+
+    def local_run(self, p) -> tuple[int, int] | None:
+        """[lo, hi) of p's flattened elements that this rank updates, or None."""
+        dtype, offset = self.place[id(p)]
+        start, stop = self.shard(dtype)
+        lo, hi = max(start, offset) - offset, min(stop, offset + p.numel()) - offset
+        return (lo, hi) if lo < hi else None
+
+
+class _ZeroMixin:
+    """ZeRO-1 behaviour for a fused StateOptimizer subclass (see module docstring)."""
+
+    def __init__(self, params, *args, process_group=None, **kwargs):
+        super().__init__(params, *args, **kwargs)
+        self._group = process_group
+        initialized = torch.distributed.is_available() and torch.distributed.is_initialized()
+        self._world = torch.distributed.get_world_size(process_group) if initialized else 1
+        self._rank = torch.distributed.get_rank(process_group) if initialized else 0
+        ordered = [p for g in self.param_groups for p in g["params"]]
+        self._layout = FlatLayout(ordered, self._world, self._rank)
+        self._events: list = []
+        self._timed: list = []
+
+    def local_numel(self) -> int:
+        total = 0
+        for g in self.param_groups:
+            for p in g["params"]:
+                run = self._layout.local_run(p)
+                total += (run[1] - run[0]) if run else 0
+        return total
+
+    def launches_per_step(self) -> int:
+        return getattr(self, "_srs_launches_last_step", 0)
+
+    def _group_items(self, group, formats, first_index):
+        names = self._state_names
+        for param_index, parameter in enumerate(group["params"], start=first_index):
+            grad = parameter.grad
+            if grad is None:
+                continue
+            if grad.is_sparse:
+                raise RuntimeError(f"{type(self).__name__} does not support sparse gradients")
+            _validate_rng_numel(parameter.numel())
+            run = self._layout.local_run(parameter)
+            if run is None:
+                continue
+            lo, hi = run
+            piece = _Piece(parameter.detach().view(-1)[lo:hi], grad.reshape(-1)[lo:hi])
+            state = self.state[parameter]
+            for name, fmt in zip(names, formats):
+                if name not in state:
+                    state[name] = torch.zeros(hi - lo, dtype=fmt.dtype, device=parameter.device)
+                elif state[name].dtype != fmt.dtype:
+                    raise ValueError(f"{name} dtype does not match its state format")
+            yield piece, state, param_index, state.get("step", 0) + 1, lo + self._shard_start(
+                parameter)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        stream = torch.cuda.current_stream() if torch.cuda.is_available() else None
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if stream else None
+        if marks:
+            marks[0].record(stream)
+        self._srs_launches = 0
+        loss = super().step(closure)
+        self._srs_launches_last_step = self._srs_launches
+        if marks:
+            marks[1].record(stream)
+        if self._world > 1:
+            for dtype, buffer in self._layout.buffers.items():
+                lo, hi = self._layout.shard(dtype)
+                torch.distributed.all_gather_into_tensor(buffer, buffer[lo:hi], group=self._group)
+        if marks:
+            marks[2].record(stream)
+            self._events.append(marks)
+        return loss
+
+    @property
+    def timings(self):
+        """Per step since the last clear: update_ms (fused kernel launches) and
+        gather_ms (all-gather); reading it synchronizes on the recorded events."""
+        for marks in self._events:
+            marks[2].synchronize()
+            self._timed.append({"update_ms": marks[0].elapsed_time(marks[1]),
+                                "gather_ms": marks[1].elapsed_time(marks[2])})
+        self._events = []
+        return _TimingList(self._timed)
+
+    def close(self):
+        self._events, self._timed = [], []
+
+
+class _TimingList(list):
+    def __init__(self, backing):
+        super().__init__(backing)
+        self._backing = backing
+
+    def clear(self):
+        super().clear()
+        self._backing.clear()
+
+
+class ZeroAdamW(_ZeroMixin, AdamWReferenceSR):
+    """AdamW (fused, sm_100a) with ZeRO-1 sharded states; see the module docstring."""
+
+
+class ZeroSGDM(_ZeroMixin, SGDMReferenceSR):
+    """Momentum SGD (fused, sm_100a) with ZeRO-1 sharded states."""
+
+
+def shard_sizes(numel_total: int, world: int) -> int:
+    """Elements per shard of a flat buffer of ``numel_total`` elements."""
+    unit = world * SHARD_ALIGN
+    return math.ceil(numel_total / unit) * unit // world

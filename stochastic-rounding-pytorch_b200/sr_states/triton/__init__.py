@@ -1,0 +1,24 @@
+"""Import-compatible names for code written against the reference's Triton backend.
+
+Every name here is the sm_100a CUDA implementation from ``sr_states.cuda``;
+no Triton code is imported or run.  ``from sr_states.triton import AdamWTriton``
+therefore keeps working unchanged.
+"""
+
+from ..cuda import AdamWCuda as AdamWTriton
+from ..cuda import SGDMCuda as SGDMTriton
+from ..cuda import cast, rn_cast_bf16, sr_cast_bf16
+from ..cuda import cuda_adamw_step_ as triton_adamw_step_
+from ..cuda import cuda_sgdm_step_ as triton_sgdm_step_
+from ..cuda import is_available as is_triton_available
+
+__all__ = [
+    "AdamWTriton",
+    "SGDMTriton",
+    "cast",
+    "is_triton_available",
+    "rn_cast_bf16",
+    "sr_cast_bf16",
+    "triton_adamw_step_",
+    "triton_sgdm_step_",
+]

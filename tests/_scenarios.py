@@ -1,0 +1,100 @@
+"""Replay the reference optimizer scenarios of tests/golden/optimizers.* through
+this package's optimizer classes and compare every step with the reference bytes.
+
+Parameters are teacher-forced: after each step's comparison the parameter is
+reset to the reference's bytes, so a one-ulp difference (PyTorch's CPU sqrt is
+not correctly rounded) never compounds.  States never depend on parameters.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from _support import (FMT, adamw_param_close, assert_bits_or_nan, from_bits, load_json, load_npz,
+                      tbits, ulp_distance)
+
+
+def scenarios():
+    return load_json("optimizers.json")["scenarios"]
+
+
+def _classes():
+    import sr_states
+
+    return {"adamw": sr_states.AdamWReferenceSR, "sgdm": sr_states.SGDMReferenceSR}
+
+
+def build(spec, arrays, device, cls=None):
+    from sr_states import StateFormat
+
+    name, names = spec["name"], spec["state_names"]
+    shapes = [(tuple(s), getattr(torch, d)) for s, d in spec["shapes"]]
+    params = [torch.nn.Parameter(from_bits(arrays[f"{name}__p{i}__init"], dt, device).reshape(s))
+              for i, (s, dt) in enumerate(shapes)]
+    groups = []
+    for g in spec["groups"]:
+        fmt = {n: StateFormat(getattr(torch, d), r) for n, (d, r) in zip(names, g["formats"])}
+        hp = dict(g["hp"])
+        if "betas" in hp:
+            hp["betas"] = tuple(hp["betas"])
+        groups.append({"params": [params[i] for i in g["params"]], "state_format": fmt,
+                       "sr_seed": g["sr_seed"], **hp})
+    cls = cls or _classes()[spec["kind"]]
+    opt = cls(groups, lr=0.01) if spec["kind"] == "sgdm" else cls(groups)
+    for tg, g in zip(opt.param_groups, spec["groups"]):
+        tg["sr_step"] = g["sr_step"]
+    for pid, init in spec["initial"].items():
+        p = params[int(pid)]
+        group = next(tg for tg in opt.param_groups if any(q is p for q in tg["params"]))
+        for n, fmt in zip(names, opt._formats(group)):
+            opt.state[p][n] = from_bits(arrays[f"{name}__p{pid}__{n}__init"], fmt.dtype,
+                                        device).reshape(p.shape)
+        opt.state[p]["step"] = init["step"]
+    return params, opt
+
+
+def replay(spec, device, cls=None, arrays=None):
+    """Run the scenario; returns (total parameter elements compared, mismatching ones)."""
+    arrays = arrays if arrays is not None else load_npz("optimizers.npz")
+    name, names, kind = spec["name"], spec["state_names"], spec["kind"]
+    params, opt = build(spec, arrays, device, cls)
+    skip = {tuple(x) for x in spec["grad_none"]}
+    compared = mismatched = 0
+    group_of = {i: g for g in spec["groups"] for i in g["params"]}
+    for step in range(1, spec["steps"] + 1):
+        previous = [tbits(p).reshape(-1).copy() for p in params]
+        for i, p in enumerate(params):
+            p.grad = None if (step, i) in skip else from_bits(
+                arrays[f"{name}__p{i}__grad{step}"], p.dtype, device).reshape(p.shape)
+        opt.step()
+        for i, p in enumerate(params):
+            context = f"{name} step {step} param {i}"
+            golden = arrays[f"{name}__p{i}__step{step}"].reshape(-1)
+            actual = tbits(p).reshape(-1)
+            width = 8 * p.element_size()
+            distance = ulp_distance(actual, golden, width)
+            if kind == "sgdm":
+                assert distance.max(initial=0) == 0, context
+            else:
+                hp = group_of[i]["hp"]
+                prev = (previous[i].view(np.float32) if width == 32
+                        else (previous[i].astype(np.uint32) << 16).view(np.float32))
+                ok = adamw_param_close(actual, golden, prev, 1.0 - hp["lr"] * hp["weight_decay"],
+                                       width)
+                assert ok.all(), f"{context}: {distance.max()} ulp"
+            compared += distance.size
+            mismatched += int(np.count_nonzero(distance))
+            for n in names:
+                key = f"{name}__p{i}__{n}__step{step}"
+                if key in arrays:
+                    st = opt.state[p][n]
+                    assert_bits_or_nan(tbits(st), arrays[key], FMT[st.dtype], f"{context} {n}")
+                else:
+                    assert n not in opt.state[p], context
+            if f"{name}__p{i}__adamstep{step}" in arrays:
+                assert opt.state[p]["step"] == int(arrays[f"{name}__p{i}__adamstep{step}"][0])
+            with torch.no_grad():  # teacher forcing
+                p.copy_(from_bits(golden, p.dtype, device).reshape(p.shape))
+    assert [g["sr_step"] for g in opt.param_groups] == spec["final_sr_step"]
+    return compared, mismatched

@@ -1,0 +1,117 @@
+"""Pin the CPU oracle to the reference: every golden vector in tests/golden/ was
+produced by running the reference itself (tests/golden/make_golden.py)."""
+
+import hashlib
+
+import numpy as np
+import pytest
+
+import oracle
+from _support import adamw_param_close, load_json, load_npz, ulp_distance
+
+
+def test_update_and_state_keys_match_reference():
+    from sr_states._hash import state_key, update_key
+
+    keys = load_json("keys.json")
+    for seed, step, index, expected in keys["update_key"]:
+        assert oracle.update_key(seed, step, index) == expected, (seed, step, index)
+        assert update_key(seed, step, index) == expected, (seed, step, index)
+    for key, index, expected in keys["state_key"]:
+        assert oracle.state_key(key, index) == expected
+        assert state_key(key, index) == expected
+    counters = np.array(keys["h32"]["counters"], dtype=np.uint64).astype(np.uint32)
+    assert np.array_equal(oracle.h32(counters), np.array(keys["h32"]["hashes"], dtype=np.uint32))
+
+
+def test_reference_known_answers():
+    # The reference's own known-answer values (tests/test_rng_streams.py:41-66).
+    assert oracle.update_key(0, 1, 0) == 0x7D2B5EA8
+    assert oracle.update_key(-1, 1 << 32, 1) == 0x03D350C7
+    assert oracle.state_key(0, 1) == 0x688990C0
+    assert oracle.state_key(0xFFFFFFFF, 2) == 0x5681FFD9
+
+
+@pytest.mark.parametrize("case", load_json("casts.json")["cases"], ids=lambda c: c["key"])
+def test_oracle_cast_matches_reference_bytes(case):
+    arrays = load_npz("casts.npz")
+    x = arrays[case["input"]].view(np.float32)
+    out = oracle.cast(x, case["format"], case["rule"], case["seed"], case["offset"])
+    # Byte-exact, NaN encodings included.
+    assert np.array_equal(out, arrays[case["key"]])
+
+
+@pytest.mark.parametrize("case", load_json("functional.json")["cases"], ids=lambda c: c["name"])
+def test_oracle_functional_step_matches_reference(case):
+    arrays = load_npz("functional.npz")
+    import torch
+
+    g = arrays["grad"].view(np.float32).copy()
+    p = torch.linspace(-1, 1, g.size).numpy().copy()  # the reference's initial parameter
+    fmt, rule, name = case["format"], case["rule"], case["name"]
+    dt = oracle.BITS_DTYPE[fmt]
+    if case["kind"] == "adamw":
+        m, v = np.zeros(g.size, dt), np.zeros(g.size, dt)
+        oracle.adamw_(p, g, m, v, m_fmt=fmt, m_rule=rule, v_fmt=fmt, v_rule=rule, lr=0.01,
+                      beta1=0.5, beta2=0.5, eps=0.125, weight_decay=0.0, step=1,
+                      update_key=case["key"], offset=case["offset"])
+        states = (m, v)
+        assert ulp_distance(p.view(np.uint32), arrays[f"{name}__param"], 32).max() <= 1
+        assert (p.view(np.uint32) == arrays[f"{name}__param"]).all()  # dyadic: sqrt exact
+    else:
+        u = np.zeros(g.size, dt)
+        oracle.sgdm_(p, g, u, u_fmt=fmt, u_rule=rule, lr=0.01, momentum=0.5,
+                     update_key=case["key"], offset=case["offset"])
+        states = (u,)
+        assert np.array_equal(p.view(np.uint32), arrays[f"{name}__param"])
+    for i, s in enumerate(states):
+        assert np.array_equal(s, arrays[f"{name}__state{i}"])
+
+
+def _config1_step(p, g, m, v, step):
+    oracle.adamw_(p, g, m, v, m_fmt=oracle.BF16, m_rule=oracle.STOCHASTIC, v_fmt=oracle.BF16,
+                  v_rule=oracle.STOCHASTIC, lr=3e-4, beta1=0.9, beta2=0.999, eps=1e-8,
+                  weight_decay=0.01, step=step, update_key=oracle.update_key(7, step, 0),
+                  offset=0, threads=4)
+
+
+def test_oracle_config1_trajectory_matches_reference():
+    """BASELINE config 1 at n = 2^13: every step teacher-forced from the reference's
+    previous bytes; states bit-exact, FP32 parameter within the sqrt tolerance."""
+    a = load_npz("config1.npz")
+    p = a["param_init"].view(np.float32).copy()
+    m = np.zeros(p.size, np.uint16)
+    v = np.zeros(p.size, np.uint16)
+    mismatched = 0
+    for step in range(1, 11):
+        g = a[f"grad_{step}"].view(np.float32).copy()
+        _config1_step(p, g, m, v, step)
+        assert np.array_equal(m, a[f"exp_avg_{step}"]), step
+        assert np.array_equal(v, a[f"exp_avg_sq_{step}"]), step
+        p_prev = a["param_init" if step == 1 else f"param_{step - 1}"].view(np.float32)
+        assert adamw_param_close(p.view(np.uint32), a[f"param_{step}"], p_prev,
+                                 1.0 - 3e-4 * 0.01, 32).all(), step
+        mismatched += int(np.count_nonzero(p.view(np.uint32) != a[f"param_{step}"]))
+        p = a[f"param_{step}"].view(np.float32).copy()
+    # PyTorch's CPU sqrt differs from a correctly rounded one on ~0.7% of inputs;
+    # ~1e-4 of parameters then differ by one ulp.
+    assert mismatched / (10 * p.size) < 2e-3
+
+
+def test_oracle_config1_full_size_state_digests():
+    """BASELINE config 1 at its full 2^20 elements: SHA-256 of the state bytes after
+    every step equals the reference's (gradients regenerated from the same seed)."""
+    import torch
+
+    spec = load_json("config1_full.json")
+    n = spec["n"]
+    gen = torch.Generator().manual_seed(spec["seed_generator"])
+    p = (torch.randn(n, generator=gen) * 0.02).numpy().copy()
+    m = np.zeros(n, np.uint16)
+    v = np.zeros(n, np.uint16)
+    for entry in spec["steps"]:
+        g = (torch.randn(n, generator=gen) * 1e-3).numpy().copy()
+        assert hashlib.sha256(g.view(np.uint32).tobytes()).hexdigest() == entry["grad_sha256"]
+        _config1_step(p, g, m, v, entry["step"])
+        assert hashlib.sha256(m.tobytes()).hexdigest() == entry["exp_avg_sha256"]
+        assert hashlib.sha256(v.tobytes()).hexdigest() == entry["exp_avg_sq_sha256"]
