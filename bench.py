@@ -52,6 +52,10 @@ def parse_args(argv=None):
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
                         help="CPU work budget of the CPU baseline sample")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--layers", type=int, default=32,
+                        help="decoder layers of the Llama-3-8B shape (profiling uses fewer)")
+    parser.add_argument("--no-embeddings", action="store_true",
+                        help="drop the two 128256x4096 matrices (profiling case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     return parser.parse_args(argv)
 
@@ -156,7 +160,7 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload --
 
-def build_workload(world, rank):
+def build_workload(world, rank, layers=32, embeddings=True):
     """Flat BF16 parameter and gradient buffers holding the 291 tensors; the
     optimizer (ZeRO-1 when world > 1) over views of them."""
     import torch
@@ -165,7 +169,9 @@ def build_workload(world, rank):
     from sr_states.distributed import ZeroAdamW
     from sr_states.shapes import llama3_8b
 
-    shapes = [s for _, s in llama3_8b()]
+    shapes = [s for name, s in llama3_8b()
+              if (embeddings or name not in ("embed_tokens", "lm_head"))
+              and not (name.startswith("layers.") and int(name.split(".")[1]) >= layers)]
     total = sum(math.prod(s) for s in shapes)
     device = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=device).manual_seed(7)
@@ -277,7 +283,8 @@ def run_b200(args):
 
     world, rank = init_distributed(args.gpus)
     peak, peak_source = measured_hbm_peak()
-    opt, params, flat_p, flat_g, total = build_workload(world, rank)
+    opt, params, flat_p, flat_g, total = build_workload(world, rank, args.layers,
+                                                        not args.no_embeddings)
     local = opt.local_numel()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -297,7 +304,9 @@ def run_b200(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4)",
+        "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4)"
+                   + ("" if (args.layers, args.no_embeddings) == (32, False)
+                      else f" reduced to {args.layers} layers, embeddings={not args.no_embeddings}"),
                    "params": total, "tensors": len(params), "param_dtype": "bf16",
                    "grad_dtype": "bf16", "exp_avg": "float8_e4m3fn stochastic",
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",

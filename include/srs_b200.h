@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define SRS_ABI_VERSION 1
+#define SRS_ABI_VERSION 2
 
 /* ---- status codes ------------------------------------------------------ */
 #define SRS_OK 0
@@ -53,6 +53,11 @@ extern "C" {
 #define SRS_ROW_VECTOR_OK 0x4u   /* every base address is aligned for 8-element vector access */
 #define SRS_ROW_CLASS_SHIFT 8    /* bits 8..15: index of the row's AdamW step class */
 #define SRS_MAX_STEP_CLASSES 32
+/* `uniform_kind` of the multi-tensor steps: the (SRS_ROW_PARAM_BF16 |
+ * SRS_ROW_GRAD_BF16) bits every row shares, or SRS_KIND_MIXED.  It selects a
+ * kernel specialised for that dtype pair; rows that do not match it still run
+ * correctly on a generic path. */
+#define SRS_KIND_MIXED 0xFFFFFFFFu
 
 /*
  * One row = one contiguous run of `numel` elements of one parameter (a whole
@@ -138,11 +143,11 @@ int srs_cast(const float* x, void* y, int64_t n, int out_format, int rule, uint3
  */
 int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
                     int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
-                    const srs_rng* rng, int grid_ctas, void* stream);
+                    const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream);
 
 int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
-                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng, int grid_ctas,
-                   void* stream);
+                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
+                   uint32_t uniform_kind, int grid_ctas, void* stream);
 
 /* ---- fused single-tensor steps ------------------------------------------
  * Replace sr_states/triton/adamw.py:160-221 (`triton_adamw_step_`) and

@@ -74,7 +74,9 @@ def _ptr(a: np.ndarray, start: int = 0) -> int:
 
 
 def _chunks(n: int, threads: int, align: int = 64):
-    threads = max(1, min(threads, (n + align - 1) // align or 1))
+    if n <= 0:
+        return [(0, 0)]
+    threads = max(1, min(threads, (n + align - 1) // align))
     step = ((n + threads - 1) // threads + align - 1) // align * align
     return [(lo, min(n, lo + step)) for lo in range(0, n, step)] or [(0, 0)]
 

@@ -1,8 +1,10 @@
 // extern "C" entry points of libsrs_b200.so (declared in include/srs_b200.h):
 // argument validation, device capability check, persistent-grid sizing and
 // dispatch from runtime formats to the kernel instantiations.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -73,9 +75,9 @@ int check_hp_classes(int n) {
   return SRS_OK;
 }
 
-using AdamWLaunch = cudaError_t (*)(const srs_row*, int64_t, int64_t, const AdamWArgs&, int,
-                                    cudaStream_t);
-using SgdmLaunch = cudaError_t (*)(const srs_row*, int64_t, int64_t, const SgdmArgs&, int,
+using AdamWLaunch = cudaError_t (*)(const srs_row*, int64_t, int64_t, int, const AdamWArgs&,
+                                    int, cudaStream_t);
+using SgdmLaunch = cudaError_t (*)(const srs_row*, int64_t, int64_t, int, const SgdmArgs&, int,
                                    cudaStream_t);
 using CastLaunch = cudaError_t (*)(const float*, void*, int64_t, uint32_t, int, int, int,
                                    cudaStream_t);
@@ -92,6 +94,54 @@ const CastLaunch kCast[5] = {&launch_cast<0>, &launch_cast<1>, &launch_cast<2>, 
                              &launch_cast<4>};
 
 int fmt_bytes(int f) { return f == SRS_FMT_F32 ? 4 : (f <= SRS_FMT_F16 ? 2 : 1); }
+
+int kind_index(uint32_t uniform_kind) { return uniform_kind <= 3u ? (int)uniform_kind : 4; }
+
+float bits_float(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+uint32_t float_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+// RN(1/c) for a positive normal float c.  The product of two floats is exact
+// in double and 1 - c*t is then exact too (Sterbenz), so the neighbour of the
+// double-rounded estimate with the smallest |1 - c*t| is the correctly rounded
+// reciprocal (no ties: 1/c is never a midpoint unless c is a power of two, and
+// then 1/c is exact).  Values outside the normal range are returned as 1/c;
+// the kernels use their IEEE division for quotients out of range anyway.
+float exact_reciprocal(float c) {
+  const float est = (float)(1.0 / (double)c);
+  if (!(c > 0.0f) || !std::isfinite(est) || est < 1.1754944e-38f) return est;
+  float best = est;
+  double best_err = 2.0;
+  for (int k = -2; k <= 2; ++k) {
+    const float t = bits_float(float_bits(est) + (uint32_t)k);
+    const double err = std::fabs(1.0 - (double)c * (double)t);
+    if (err < best_err) {
+      best_err = err;
+      best = t;
+    }
+  }
+  return best;
+}
+
+// Per step class: the exact reciprocal of bias2_sqrt and the numerator range
+// [2^-59, 2^60) of the reciprocal division (empty unless 2^-30 <= c <= 2^30).
+void fill_reciprocals(const srs_adamw_hparams& hp, AdamWArgs& a) {
+  for (int c = 0; c < hp.n_step_classes; ++c) {
+    const float b = hp.bias2_sqrt[c];
+    a.inv_bias2_sqrt[c] = exact_reciprocal(b);
+    const bool ok = b >= 0x1p-30f && b <= 0x1p30f;
+    a.fast_lo[c] = ok ? 0x22000000u : 0u;
+    a.fast_hi[c] = ok ? 0x5D800000u : 0u;
+  }
+}
 
 __global__ void derive_keys_kernel(const uint32_t* __restrict__ index, uint32_t* __restrict__ out,
                                    int64_t n, const srs_rng rng) {
@@ -187,7 +237,7 @@ static int check_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, con
 
 int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
                     int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
-                    const srs_rng* rng, int grid_ctas, void* stream) {
+                    const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream) {
   g_error[0] = '\0';
   if (!valid_format(m_format) || !valid_format(v_format))
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format (%d, %d)", m_format, v_format);
@@ -199,17 +249,19 @@ int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_
   if (int rc = check_device()) return rc;
   AdamWArgs a{};
   a.hp = *hp;
+  fill_reciprocals(*hp, a);
   a.rng = *rng;
   a.m_stochastic = m_rule;
   a.v_stochastic = v_rule;
-  const cudaError_t e = kAdamW[m_format][v_format](rows, n_rows, n_tiles, a, grid_ctas,
+  const cudaError_t e = kAdamW[m_format][v_format](rows, n_rows, n_tiles,
+                                                   kind_index(uniform_kind), a, grid_ctas,
                                                    static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_multi launch");
 }
 
 int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
-                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng, int grid_ctas,
-                   void* stream) {
+                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
+                   uint32_t uniform_kind, int grid_ctas, void* stream) {
   g_error[0] = '\0';
   if (!valid_format(u_format))
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format %d", u_format);
@@ -221,8 +273,8 @@ int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_f
   a.hp = *hp;
   a.rng = *rng;
   a.u_stochastic = u_rule;
-  const cudaError_t e =
-      kSgdm[u_format](rows, n_rows, n_tiles, a, grid_ctas, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = kSgdm[u_format](rows, n_rows, n_tiles, kind_index(uniform_kind), a,
+                                        grid_ctas, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_sgdm_multi launch");
 }
 
@@ -256,10 +308,12 @@ int srs_adamw_single(const srs_row* row, int m_format, int m_rule, int v_format,
   a.inline_row.tile_begin = 0;
   a.inline_row.flags &= ~(0xFFu << SRS_ROW_CLASS_SHIFT);
   a.hp = *hp;
+  fill_reciprocals(*hp, a);
   a.rng.key_mode = SRS_KEY_GIVEN;
   a.m_stochastic = m_rule;
   a.v_stochastic = v_rule;
-  const cudaError_t e = kAdamW[m_format][v_format](nullptr, 1, n_tiles, a, grid_ctas,
+  const cudaError_t e = kAdamW[m_format][v_format](nullptr, 1, n_tiles, (int)(row->flags & 3u),
+                                                   a, grid_ctas,
                                                    static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_single launch");
 }
@@ -282,8 +336,8 @@ int srs_sgdm_single(const srs_row* row, int u_format, int u_rule, const srs_sgdm
   a.hp = *hp;
   a.rng.key_mode = SRS_KEY_GIVEN;
   a.u_stochastic = u_rule;
-  const cudaError_t e =
-      kSgdm[u_format](nullptr, 1, n_tiles, a, grid_ctas, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = kSgdm[u_format](nullptr, 1, n_tiles, (int)(row->flags & 3u), a,
+                                        grid_ctas, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_sgdm_single launch");
 }
 

@@ -8,19 +8,31 @@
 
 namespace srs {
 
-template <int MF, int VF>
-cudaError_t launch_adamw(const srs_row* rows, int64_t n_rows, int64_t n_tiles,
-                         const AdamWArgs& a, int grid_ctas, cudaStream_t stream) {
+template <int MF, int VF, int KIND>
+static cudaError_t launch_kind(const srs_row* rows, int64_t n_rows, int64_t n_tiles,
+                               const AdamWArgs& a, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
-  const int grid = grid_for(reinterpret_cast<const void*>(&adamw_kernel<MF, VF>), n_tiles,
+  const int grid = grid_for(reinterpret_cast<const void*>(&adamw_kernel<MF, VF, KIND>), n_tiles,
                             grid_ctas, &err);
   if (err != cudaSuccess) return err;
-  adamw_kernel<MF, VF><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
+  adamw_kernel<MF, VF, KIND><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
   return cudaGetLastError();
 }
 
-#define SRS_INSTANTIATE(VF)                                                               \
-  template cudaError_t launch_adamw<SRS_M_FORMAT, VF>(const srs_row*, int64_t, int64_t, \
+template <int MF, int VF>
+cudaError_t launch_adamw(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int kind,
+                         const AdamWArgs& a, int grid_ctas, cudaStream_t stream) {
+  switch (kind) {
+    case 0: return launch_kind<MF, VF, 0>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    case 1: return launch_kind<MF, VF, 1>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    case 2: return launch_kind<MF, VF, 2>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    case 3: return launch_kind<MF, VF, 3>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    default: return launch_kind<MF, VF, kKindMixed>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+  }
+}
+
+#define SRS_INSTANTIATE(VF)                                                                  \
+  template cudaError_t launch_adamw<SRS_M_FORMAT, VF>(const srs_row*, int64_t, int64_t, int, \
                                                       const AdamWArgs&, int, cudaStream_t);
 SRS_INSTANTIATE(SRS_FMT_F32)
 SRS_INSTANTIATE(SRS_FMT_BF16)

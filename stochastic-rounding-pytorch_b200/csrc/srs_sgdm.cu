@@ -3,19 +3,31 @@
 
 namespace srs {
 
-template <int UF>
-cudaError_t launch_sgdm(const srs_row* rows, int64_t n_rows, int64_t n_tiles, const SgdmArgs& a,
-                        int grid_ctas, cudaStream_t stream) {
+template <int UF, int KIND>
+static cudaError_t launch_kind(const srs_row* rows, int64_t n_rows, int64_t n_tiles,
+                               const SgdmArgs& a, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
-  const int grid =
-      grid_for(reinterpret_cast<const void*>(&sgdm_kernel<UF>), n_tiles, grid_ctas, &err);
+  const int grid = grid_for(reinterpret_cast<const void*>(&sgdm_kernel<UF, KIND>), n_tiles,
+                            grid_ctas, &err);
   if (err != cudaSuccess) return err;
-  sgdm_kernel<UF><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
+  sgdm_kernel<UF, KIND><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
   return cudaGetLastError();
 }
 
-#define SRS_INSTANTIATE(UF)                                                              \
-  template cudaError_t launch_sgdm<UF>(const srs_row*, int64_t, int64_t, const SgdmArgs&, \
+template <int UF>
+cudaError_t launch_sgdm(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int kind,
+                        const SgdmArgs& a, int grid_ctas, cudaStream_t stream) {
+  switch (kind) {
+    case 0: return launch_kind<UF, 0>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    case 1: return launch_kind<UF, 1>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    case 2: return launch_kind<UF, 2>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    case 3: return launch_kind<UF, 3>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+    default: return launch_kind<UF, kKindMixed>(rows, n_rows, n_tiles, a, grid_ctas, stream);
+  }
+}
+
+#define SRS_INSTANTIATE(UF)                                                                   \
+  template cudaError_t launch_sgdm<UF>(const srs_row*, int64_t, int64_t, int, const SgdmArgs&, \
                                        int, cudaStream_t);
 SRS_INSTANTIATE(SRS_FMT_F32)
 SRS_INSTANTIATE(SRS_FMT_BF16)

@@ -26,6 +26,7 @@ ROW_GRAD_BF16 = 0x2
 ROW_VECTOR_OK = 0x4
 ROW_CLASS_SHIFT = 8
 MAX_STEP_CLASSES = 32
+KIND_MIXED = 0xFFFFFFFF
 KEY_DERIVE = 0
 KEY_GIVEN = 1
 
@@ -75,10 +76,11 @@ _SIGNATURES = {
                   ctypes.c_uint32, ctypes.c_int, _P], ctypes.c_int),
     "srs_adamw_multi": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                          ctypes.c_int, ctypes.c_int, ctypes.POINTER(SrsAdamWHparams),
-                         ctypes.POINTER(SrsRng), ctypes.c_int, _P], ctypes.c_int),
+                         ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.c_int, _P],
+                        ctypes.c_int),
     "srs_sgdm_multi": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
-                        ctypes.POINTER(SrsSgdmHparams), ctypes.POINTER(SrsRng), ctypes.c_int,
-                        _P], ctypes.c_int),
+                        ctypes.POINTER(SrsSgdmHparams), ctypes.POINTER(SrsRng), ctypes.c_uint32,
+                        ctypes.c_int, _P], ctypes.c_int),
     "srs_adamw_single": ([ctypes.POINTER(SrsRow), ctypes.c_int, ctypes.c_int, ctypes.c_int,
                           ctypes.c_int, ctypes.POINTER(SrsAdamWHparams), ctypes.c_int, _P],
                          ctypes.c_int),
@@ -86,7 +88,7 @@ _SIGNATURES = {
                          ctypes.POINTER(SrsSgdmHparams), ctypes.c_int, _P], ctypes.c_int),
     "srs_derive_keys": ([_P, _P, ctypes.c_int64, ctypes.POINTER(SrsRng), _P], ctypes.c_int),
 }
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lock = threading.Lock()
 _library = None
@@ -156,12 +158,12 @@ class NativeLauncher:
                     grid_ctas=0):
         _check(load_library().srs_adamw_multi(table.device_ptr, n_rows, n_tiles, m_fmt, m_rule,
                                               v_fmt, v_rule, ctypes.byref(hp), ctypes.byref(rng),
-                                              grid_ctas, stream))
+                                              table.uniform_kind, grid_ctas, stream))
 
     def sgdm_multi(self, table, n_rows, n_tiles, u_fmt, u_rule, hp, rng, stream, grid_ctas=0):
         _check(load_library().srs_sgdm_multi(table.device_ptr, n_rows, n_tiles, u_fmt, u_rule,
-                                             ctypes.byref(hp), ctypes.byref(rng), grid_ctas,
-                                             stream))
+                                             ctypes.byref(hp), ctypes.byref(rng),
+                                             table.uniform_kind, grid_ctas, stream))
 
     def adamw_single(self, row, m_fmt, m_rule, v_fmt, v_rule, hp, stream, grid_ctas=0):
         _check(load_library().srs_adamw_single(ctypes.byref(row), m_fmt, m_rule, v_fmt, v_rule,

@@ -65,6 +65,12 @@ class DeviceTable:
     def device_ptr(self) -> int:
         return self.storage.data_ptr()
 
+    @property
+    def uniform_kind(self) -> int:
+        """Parameter/gradient dtype bits shared by every row, or KIND_MIXED."""
+        kinds = np.unique(self.host["flags"] & (_native.ROW_PARAM_BF16 | _native.ROW_GRAD_BF16))
+        return int(kinds[0]) if kinds.size == 1 else _native.KIND_MIXED
+
 
 @dataclass(frozen=True)
 class Launch:

@@ -73,7 +73,7 @@ int main(void) {{
 
 def test_library_information_without_a_gpu():
     lib = _native.load_library()
-    assert lib.srs_abi_version() == 1
+    assert lib.srs_abi_version() == 2
     assert lib.srs_tile_elems() == 2048
 
 
@@ -88,16 +88,19 @@ def test_invalid_arguments_fail_with_text_and_touch_no_device():
     hp = _native.SrsAdamWHparams()
     rng = _native.SrsRng()
     hp.n_step_classes = 0
-    rc = lib.srs_adamw_multi(None, 0, 0, 1, 1, 1, 1, ctypes.byref(hp), ctypes.byref(rng), 0, None)
+    rc = lib.srs_adamw_multi(None, 0, 0, 1, 1, 1, 1, ctypes.byref(hp), ctypes.byref(rng),
+                             _native.KIND_MIXED, 0, None)
     assert rc == _native.SRS_ERR_INVALID_ARGUMENT and b"n_step_classes" in lib.srs_last_error()
     hp.n_step_classes = 1
     rng.key_mode = 5
-    rc = lib.srs_adamw_multi(None, 0, 0, 1, 1, 1, 1, ctypes.byref(hp), ctypes.byref(rng), 0, None)
+    rc = lib.srs_adamw_multi(None, 0, 0, 1, 1, 1, 1, ctypes.byref(hp), ctypes.byref(rng), 0, 0,
+                             None)
     assert rc == _native.SRS_ERR_INVALID_ARGUMENT and b"key_mode" in lib.srs_last_error()
     rng.key_mode = 0
-    rc = lib.srs_adamw_multi(None, 0, 4, 1, 1, 1, 1, ctypes.byref(hp), ctypes.byref(rng), 0, None)
+    rc = lib.srs_adamw_multi(None, 0, 4, 1, 1, 1, 1, ctypes.byref(hp), ctypes.byref(rng), 3, 0,
+                             None)
     assert rc == _native.SRS_ERR_INVALID_ARGUMENT and b"without rows" in lib.srs_last_error()
-    rc = lib.srs_sgdm_multi(None, 0, 0, 6, 1, None, None, 0, None)
+    rc = lib.srs_sgdm_multi(None, 0, 0, 6, 1, None, None, 0, 0, None)
     assert rc == _native.SRS_ERR_INVALID_ARGUMENT
     row = _native.SrsRow()
     row.numel = -1

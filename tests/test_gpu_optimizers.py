@@ -266,3 +266,31 @@ def test_device_keys_match_host(seed, step, cuda_device):
     for i, idx in enumerate([0, 1, 2**31 + 1, 2**32 - 1]):
         k = update_key(seed, step, idx)
         assert got[i] == [k, state_key(k, 0), state_key(k, 1)]
+
+
+@pytest.mark.parametrize("beta2,step", [(0.999, 1), (0.999, 1000), (0.95, 3), (0.0, 1),
+                                        (1 - 2.0**-40, 2)])
+def test_adamw_denominator_over_every_exponent_matches_oracle(beta2, step, cuda_device):
+    """v' spans every FP32 exponent (plus 0, Inf, NaN), so sqrt(v')/sqrt(bc2) takes
+    both the reciprocal-division path and the IEEE fallback; bit-exact vs the oracle."""
+    from sr_states.cuda import cuda_adamw_step_
+
+    exps = torch.arange(-149, 128, dtype=torch.float64)
+    mant = torch.linspace(1.0, 1.999, 37, dtype=torch.float64)
+    v = (torch.exp2(exps)[:, None] * mant[None, :]).reshape(-1).float()
+    v = torch.cat((v, torch.tensor([0.0, float("inf"), float("nan"), 3.4e38])))
+    n = v.numel()
+    gen = torch.Generator().manual_seed(int(step))
+    g = torch.randn(n, generator=gen) * torch.exp2(torch.randint(-60, 60, (n,), generator=gen))
+    g[::5] = 0.0
+    m = torch.randn(n, generator=gen)
+    p = torch.randn(n, generator=gen)
+    opts = dict(lr=1e-3, beta1=0.9, beta2=beta2, eps=1e-8, weight_decay=0.01, step=step)
+    host = [t.numpy().copy() for t in (p, g, m, v)]
+    oracle.adamw_(host[0], host[1], host[2].view(np.uint32), host[3].view(np.uint32),
+                  m_fmt=oracle.F32, m_rule=0, v_fmt=oracle.F32, v_rule=0, update_key=9,
+                  offset=0, **opts)
+    dev = [t.to(cuda_device) for t in (p, g, m, v)]
+    cuda_adamw_step_(*dev, seed=9, rounding="nearest", **opts)
+    for got, want in zip(dev, host):
+        assert_bits_or_nan(tbits(got), want.view(np.uint32), oracle.F32)

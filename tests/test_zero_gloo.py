@@ -1,0 +1,105 @@
+"""ZeRO-1 on CPU ranks (gloo, world size 2 and 3): sharded fused steps plus the
+all-gather reproduce the unsharded step byte for byte, and each rank holds
+exactly its slice of the states.  Kernel launches run the oracle stand-in."""
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem():
+    from sr_states import StateFormat
+
+    torch.manual_seed(1234)
+    shapes = [(37, 5), (129,), (1000,), (3,), (2049,), (64, 64)]
+    params = [torch.nn.Parameter(torch.randn(s).to(torch.bfloat16 if i % 2 else torch.float32))
+              for i, s in enumerate(shapes)]
+    grads = [[torch.randn(s).to(p.dtype) for p, s in zip(params, shapes)] for _ in range(3)]
+    grads[1][2] = None  # a skipped gradient still consumes its parameter index
+    fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn), "exp_avg_sq": StateFormat(torch.bfloat16)}
+    return params, grads, fmt
+
+
+def _run(cls, params, grads, fmt, **kw):
+    opt = cls([{"params": params[:3]}, {"params": params[3:], "weight_decay": 0.0}], lr=1e-2,
+              state_format=fmt, seed=2**40 + 3, **kw)
+    for step_grads in grads:
+        for p, g in zip(params, step_grads):
+            p.grad = None if g is None else g.clone()
+        opt.step()
+    return opt
+
+
+def _worker(rank, world, port, queue):
+    sys.path[:0] = [str(ROOT), str(ROOT / "stochastic-rounding-pytorch_b200"), str(ROOT / "tests")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    from _support import FakeLauncher
+    from sr_states import AdamWReferenceSR
+    from sr_states.cuda import _native
+    from sr_states.distributed import ZeroAdamW
+
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        _native.set_launcher(FakeLauncher())
+        params, grads, fmt = _problem()
+        reference = [torch.nn.Parameter(p.detach().clone()) for p in params]
+        ref_opt = _run(AdamWReferenceSR, reference, grads, fmt)
+        sharded = _run(ZeroAdamW, params, grads, fmt)
+        for p, q in zip(params, reference):
+            assert torch.equal(p.detach().view(torch.uint8), q.detach().view(torch.uint8))
+        covered = 0
+        for p, q in zip(params, reference):
+            run = sharded._layout.local_run(p)
+            if run is None:
+                assert "exp_avg" not in sharded.state[p]
+                continue
+            lo, hi = run
+            covered += hi - lo
+            for name in ("exp_avg", "exp_avg_sq"):
+                mine = sharded.state[p][name].view(torch.uint8)
+                full = ref_opt.state[q][name].reshape(-1)[lo:hi].view(torch.uint8)
+                assert torch.equal(mine, full), (rank, name)
+            assert sharded.state[p]["step"] == ref_opt.state[q]["step"]
+        total = torch.tensor([covered])
+        dist.all_reduce(total)
+        assert total.item() == sum(p.numel() for p in params)
+        queue.put((rank, "ok"))
+    except BaseException as exc:  # report, never hang the parent
+        queue.put((rank, repr(exc)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_zero1_sharded_steps_equal_unsharded(world):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results == {r: "ok" for r in range(world)}, results
