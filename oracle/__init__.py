@@ -65,6 +65,9 @@ def lib() -> ctypes.CDLL:
         handle.srs_o_sgdm_core.argtypes = [vp, i32, vp, i32, vp, i32, i32, i64, ctypes.c_float,
                                            ctypes.c_float, u32, u32]
         handle.srs_o_sgdm_core.restype = None
+        handle.srs_o_check_uniform_division.argtypes = [ctypes.c_float, ctypes.c_float, u32, u32,
+                                                         u32, u32, u32, vp]
+        handle.srs_o_check_uniform_division.restype = ctypes.c_uint64
         _lib = handle
     return _lib
 
@@ -227,3 +230,11 @@ def sgdm_core_at(p_addr, p_bf16, g_addr, g_bf16, u_addr, u_fmt, u_rule, n, momen
 
 def cast_at(x_addr, y_addr, n, fmt, rule, seed, offset) -> None:
     lib().srs_o_cast(x_addr, y_addr, n, fmt, rule, int(seed) & _MASK32, int(offset) & _MASK32)
+
+
+def check_uniform_division(c, y, first, last, stride, lo, hi):
+    """(mismatches, numerators checked) of the reciprocal division; see srs_oracle.c."""
+    checked = np.zeros(1, dtype=np.uint64)
+    bad = lib().srs_o_check_uniform_division(float(c), float(y), first, last, stride, lo, hi,
+                                             _ptr(checked))
+    return int(bad), int(checked[0])

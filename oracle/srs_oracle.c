@@ -324,3 +324,24 @@ void srs_o_sgdm(void* p, int p_bf16, const void* g, int g_bf16, void* u, int u_f
   srs_o_sgdm_core(p, p_bf16, g, g_bf16, u, u_fmt, u_rule, n, (float)momentum, (float)(-lr),
                   update_key, offset);
 }
+
+/* Check of the sm_100a kernels' division by a launch-uniform c (Markstein's
+ * correction with y = RN(1/c)): over numerators with encodings
+ * first, first+stride, ... < last, and inside the kernel's guard
+ * lo <= bits(s) < hi, count quotients that differ from the IEEE division s/c. */
+uint64_t srs_o_check_uniform_division(float c, float y, uint32_t first, uint32_t last,
+                                      uint32_t stride, uint32_t lo, uint32_t hi,
+                                      uint64_t* checked) {
+  uint64_t bad = 0, n = 0;
+  for (uint64_t u = first; u < last; u += stride) {
+    if ((uint32_t)u - lo >= hi - lo) continue;
+    const float s = u2f((uint32_t)u);
+    const float q0 = s * y;
+    const float r = fmaf(-c, q0, s);
+    const float q1 = fmaf(r, y, q0);
+    ++n;
+    if (f2u(q1) != f2u(s / c)) ++bad;
+  }
+  *checked = n;
+  return bad;
+}

@@ -24,6 +24,8 @@ CSRC = HERE / "csrc"
 INCLUDE = REPO / "include"
 BUILD = HERE / "_build"
 LIBRARY = HERE / "sr_states" / "_native" / "libsrs_b200.so"
+# Test-only kernels that check device building blocks (loaded by tests/ only).
+SELFTEST = HERE / "sr_states" / "_native" / "libsrs_selftest.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = [
@@ -57,7 +59,7 @@ def _sources() -> list[Path]:
 
 
 def up_to_date() -> bool:
-    if not LIBRARY.exists():
+    if not LIBRARY.exists() or not SELFTEST.exists():
         return False
     built = LIBRARY.stat().st_mtime
     return all(src.stat().st_mtime <= built for src in _sources() + [Path(__file__)])
@@ -94,7 +96,21 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     if result.returncode != 0:
         raise RuntimeError(f"link failed:\n{result.stderr}")
     os.replace(tmp, LIBRARY)
+    _link_selftest(verbose)
     return LIBRARY
+
+
+def _link_selftest(verbose: bool) -> None:
+    log = _compile(("srs_selftest", "srs_selftest.cu", []), verbose)
+    if verbose:
+        print(f"== srs_selftest\n{log}", file=sys.stderr)
+    tmp = SELFTEST.with_suffix(".so.tmp")
+    cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp),
+           str(BUILD / "srs_selftest.o")]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(f"link failed:\n{result.stderr}")
+    os.replace(tmp, SELFTEST)
 
 
 if __name__ == "__main__":

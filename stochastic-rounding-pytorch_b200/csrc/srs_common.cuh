@@ -23,6 +23,53 @@ constexpr int kThreads = 256;              // CTA size of every kernel
 constexpr int kVec = 8;                    // elements per thread per tile
 constexpr int64_t kTile = kThreads * kVec; // elements per tile (row table unit)
 
+// ------------------------------------------------------ packed FP32 math --
+//
+// Two-lane FP32 arithmetic on sm_100 (add/mul/fma .f32x2 on a 64-bit register
+// pair), each lane rounded to nearest once.  Measured on B200 with CUDA 12.9:
+// a packed multiply whose only use is a packed add IS fused into one FMA, even
+// with the explicit .rn modifier (and so is CUDA's __fadd2_rn(__fmul2_rn())).
+// So a product that must be rounded before an addition never goes through
+// these helpers: such pairs use mul_add_rn2 below (scalar __fmul_rn/__fadd_rn,
+// which CUDA documents as never merged).  A packed product feeding an FMA
+// operand, or an FMA result feeding an add, cannot be fused and is safe.
+
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// a*b + c with one rounding per lane.
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+      "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// RN(RN(a*b) + c) per lane: the product is rounded before the addition.
+__device__ __forceinline__ float2 mul_add_rn2(float2 a, float2 b, float2 c) {
+  return make_float2(__fadd_rn(__fmul_rn(a.x, b.x), c.x), __fadd_rn(__fmul_rn(a.y, b.y), c.y));
+}
+
 // ---------------------------------------------------------------- hashing --
 
 __device__ __forceinline__ uint32_t h32(uint32_t x) {

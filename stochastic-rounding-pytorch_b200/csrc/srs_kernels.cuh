@@ -8,8 +8,8 @@
 // (uniform_kind); rows of another pair, tails and unaligned rows go through
 // one generic, out-of-line path.
 //
-// FP32 arithmetic uses sm_100's packed two-lane instructions (__fmul2_rn,
-// __ffma2_rn, __fadd2_rn: each lane rounded to nearest on its own, never
+// FP32 arithmetic uses sm_100's packed two-lane instructions (mul2_rn,
+// fma2_rn, add2_rn: each lane rounded to nearest on its own, never
 // contracted), so the operation order is exactly the reference's.
 #pragma once
 
@@ -140,9 +140,9 @@ __device__ __forceinline__ float2 splat(float x) { return make_float2(x, x); }
 // stay far from the subnormal and overflow ranges.  Everything else (zero,
 // tiny, huge, Inf, NaN numerators) takes the IEEE division.
 __device__ __forceinline__ float2 div_by_uniform(float2 s, const ClassScalars& k) {
-  const float2 q0 = __fmul2_rn(s, splat(k.inv_c));
-  const float2 r = __ffma2_rn(splat(-k.c), q0, s);
-  const float2 q1 = __ffma2_rn(r, splat(k.inv_c), q0);
+  const float2 q0 = mul2_rn(s, splat(k.inv_c));
+  const float2 r = fma2_rn(splat(-k.c), q0, s);
+  const float2 q1 = fma2_rn(r, splat(k.inv_c), q0);
   const uint32_t bx = __float_as_uint(s.x) - k.fast_lo;
   const uint32_t by = __float_as_uint(s.y) - k.fast_lo;
   if (max(bx, by) < k.fast_span) return q1;
@@ -169,14 +169,14 @@ __device__ __forceinline__ void adamw8(const RowView& rv, int64_t e0, int count,
 #pragma unroll
   for (int i = 0; i < kVec / 2; ++i) {
     const float2 g2 = make_float2(g[2 * i], g[2 * i + 1]);
-    const float2 m1 = __ffma2_rn(g2, omb1, __fmul2_rn(make_float2(m[2 * i], m[2 * i + 1]), b1));
-    const float2 v1 = __ffma2_rn(__fmul2_rn(omb2, g2), g2,
-                                 __fmul2_rn(make_float2(v[2 * i], v[2 * i + 1]), b2));
+    const float2 m1 = fma2_rn(g2, omb1, mul2_rn(make_float2(m[2 * i], m[2 * i + 1]), b1));
+    const float2 v1 = fma2_rn(mul2_rn(omb2, g2), g2,
+                                 mul2_rn(make_float2(v[2 * i], v[2 * i + 1]), b2));
     const float2 root = make_float2(__fsqrt_rn(v1.x), __fsqrt_rn(v1.y));
-    const float2 den = __fadd2_rn(div_by_uniform(root, k), eps);
-    const float2 num = __fmul2_rn(nss, m1);
+    const float2 den = add2_rn(div_by_uniform(root, k), eps);
+    const float2 num = mul2_rn(nss, m1);
     const float2 upd = make_float2(__fdiv_rn(num.x, den.x), __fdiv_rn(num.y, den.y));
-    const float2 p1 = __fadd2_rn(__fmul2_rn(make_float2(p[2 * i], p[2 * i + 1]), decay), upd);
+    const float2 p1 = mul_add_rn2(make_float2(p[2 * i], p[2 * i + 1]), decay, upd);
     p[2 * i] = p1.x;
     p[2 * i + 1] = p1.y;
     m[2 * i] = m1.x;
@@ -255,9 +255,9 @@ __device__ __forceinline__ void sgdm8(const RowView& rv, int64_t e0, int count,
   const float2 mf = splat(a.hp.momentum), nlr = splat(a.hp.neg_lr);
 #pragma unroll
   for (int i = 0; i < kVec / 2; ++i) {
-    const float2 u1 = __fadd2_rn(__fmul2_rn(make_float2(u[2 * i], u[2 * i + 1]), mf),
-                                 make_float2(g[2 * i], g[2 * i + 1]));
-    const float2 p1 = __ffma2_rn(u1, nlr, make_float2(p[2 * i], p[2 * i + 1]));
+    const float2 u1 = mul_add_rn2(make_float2(u[2 * i], u[2 * i + 1]), mf,
+                                  make_float2(g[2 * i], g[2 * i + 1]));
+    const float2 p1 = fma2_rn(u1, nlr, make_float2(p[2 * i], p[2 * i + 1]));
     p[2 * i] = p1.x;
     p[2 * i + 1] = p1.y;
     u[2 * i] = u1.x;

@@ -1,0 +1,57 @@
+// Self-test kernels for the GPU test suite (built into libsrs_selftest.so, never
+// loaded by the package).  They check device building blocks of the product
+// kernels element by element against CUDA's correctly rounded scalar
+// intrinsics, on inputs generated on the device from a counter hash.
+#include "srs_kernels.cuh"
+
+namespace {
+
+__device__ __forceinline__ float random_float(uint32_t i, uint32_t seed, uint32_t salt) {
+  return __uint_as_float(srs::h32(srs::h32(i ^ salt) + seed));
+}
+
+__device__ __forceinline__ bool same(float a, float b) {
+  return __float_as_uint(a) == __float_as_uint(b) || (a != a && b != b);
+}
+
+// counts[0..2]: mul2, add2, fma2 vs the scalar _rn intrinsics; counts[3]:
+// mul_add_rn2 (single-use product, as in the kernels) vs separate rounding;
+// counts[4]: add2_rn(mul2_rn()) with a single-use product and counts[5]:
+// __fadd2_rn(__fmul2_rn()) -- diagnostics of the packed fusion hazard.
+__global__ void packed_math_kernel(uint64_t n, uint32_t seed, unsigned long long* counts) {
+  unsigned long long local[6] = {0, 0, 0, 0, 0, 0};
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t k = (uint32_t)i;
+    const float2 a = make_float2(random_float(k, seed, 1), random_float(k, seed, 2));
+    const float2 b = make_float2(random_float(k, seed, 3), random_float(k, seed, 4));
+    const float2 c = make_float2(random_float(k, seed, 5), random_float(k, seed, 6));
+    const float2 m = srs::mul2_rn(a, b), s = srs::add2_rn(a, b), f = srs::fma2_rn(a, b, c);
+    // Single-use products, distinct operands (c, a) so no product is shared.
+    const float2 seq = srs::mul_add_rn2(c, b, a);
+    const float2 packed_seq = srs::add2_rn(srs::mul2_rn(c, a), b);
+    const float2 cuda_seq = __fadd2_rn(__fmul2_rn(b, c), a);
+    local[0] += !same(m.x, __fmul_rn(a.x, b.x)) + !same(m.y, __fmul_rn(a.y, b.y));
+    local[1] += !same(s.x, __fadd_rn(a.x, b.x)) + !same(s.y, __fadd_rn(a.y, b.y));
+    local[2] += !same(f.x, __fmaf_rn(a.x, b.x, c.x)) + !same(f.y, __fmaf_rn(a.y, b.y, c.y));
+    // Reference: the exact product (a double holds it), rounded to float, then one
+    // rounded addition.
+    const float sx = __fadd_rn(__double2float_rn((double)c.x * b.x), a.x);
+    const float sy = __fadd_rn(__double2float_rn((double)c.y * b.y), a.y);
+    local[3] += !same(seq.x, sx) + !same(seq.y, sy);
+    local[4] += !same(packed_seq.x, __fadd_rn(__double2float_rn((double)c.x * a.x), b.x)) +
+                !same(packed_seq.y, __fadd_rn(__double2float_rn((double)c.y * a.y), b.y));
+    local[5] += !same(cuda_seq.x, __fadd_rn(__double2float_rn((double)b.x * c.x), a.x)) +
+                !same(cuda_seq.y, __fadd_rn(__double2float_rn((double)b.y * c.y), a.y));
+  }
+  for (int j = 0; j < 6; ++j)
+    if (local[j]) atomicAdd(&counts[j], local[j]);
+}
+
+}  // namespace
+
+extern "C" int srs_selftest_packed_math(uint64_t n, uint32_t seed, unsigned long long* counts,
+                                        void* stream) {
+  packed_math_kernel<<<592, 256, 0, static_cast<cudaStream_t>(stream)>>>(n, seed, counts);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
