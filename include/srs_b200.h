@@ -149,6 +149,29 @@ int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_f
                    int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
                    uint32_t uniform_kind, int grid_ctas, void* stream);
 
+/* ---- multi-tensor AdamW step that allocates nothing ----------------------
+ * No counterpart in the reference.  Same update as srs_adamw_multi, for
+ * callers that cannot allocate device memory at step time (a runtime whose
+ * allocator is reserved or already full, or a step issued from code that must
+ * not call into any allocator).  `host_rows` is a HOST array of n_rows srs_row,
+ * copied on `stream` into a fixed device-resident table of
+ * SRS_NOALLOC_MAX_ROWS rows that every call on a device shares.  Pageable
+ * host_rows may be reused once the call returns; page-locked host_rows must
+ * stay unchanged until the step has run on the stream.  The parameter/gradient
+ * dtype kind is read from the rows.
+ * Limits and rules:
+ *   - n_rows > SRS_NOALLOC_MAX_ROWS fails with SRS_ERR_INVALID_ARGUMENT;
+ *   - the first call on a device looks up the table's address (set-up); make
+ *     that first call before any stream capture;
+ *   - calls on one device that can overlap in time (different streams or host
+ *     threads without ordering) race on the shared table: order them.
+ */
+#define SRS_NOALLOC_MAX_ROWS 4096
+int srs_adamw_multi_noalloc(const srs_row* host_rows, int64_t n_rows, int64_t n_tiles,
+                            int m_format, int m_rule, int v_format, int v_rule,
+                            const srs_adamw_hparams* hp, const srs_rng* rng, int grid_ctas,
+                            void* stream);
+
 /* ---- fused single-tensor steps ------------------------------------------
  * Replace sr_states/triton/adamw.py:160-221 (`triton_adamw_step_`) and
  * sr_states/triton/sgd.py:115-171 (`triton_sgdm_step_`).  `row` is a HOST

@@ -357,3 +357,122 @@ int srs_derive_keys(const uint32_t* param_index, uint32_t* out, int64_t n, const
 }
 
 }  // extern "C"
+
+// ---- srs_adamw_multi_noalloc ------------------------------------------------
+// The multi-tensor AdamW step for callers that must not allocate device memory
+// while stepping: a runtime whose device memory is reserved up front (a
+// serving or training process that hands the whole HBM to its own arena), or
+// code running where an allocator call could block or fail.  srs_adamw_multi
+// needs its row table in device memory that the caller allocated; this entry
+// point instead copies a host row table into the fixed table below, which is
+// part of the library's device image (one instance per device, loaded with the
+// module), and launches the same kernel on it.
+//
+// The table is the only scratch the step uses.  Every call on a device shares
+// it and leaves its own rows in it; nothing in it has to start at zero, as a
+// call writes rows [0, n_rows) before its kernel reads them and the kernel
+// reads no row beyond n_rows.  Two calls whose copies and kernels can overlap
+// in time (different streams, or host threads without ordering) race on it.
+static __device__ __align__(256) srs_row g_noalloc_rows[SRS_NOALLOC_MAX_ROWS];
+
+namespace srs {
+namespace {
+
+srs_row* g_noalloc_table[kMaxDevices];  // device address of g_noalloc_rows, per device
+
+// Set-up on a device's first call: look up where the module placed the table.
+// Module loading is lazy, so this first lookup may load the library's device
+// code; make the first call on each device before any stream capture.
+int noalloc_table(srs_row** table) {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_noalloc_table[dev] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&address, g_noalloc_rows);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(row table)");
+    g_noalloc_table[dev] = static_cast<srs_row*>(address);
+  }
+  *table = g_noalloc_table[dev];
+  return SRS_OK;
+}
+
+// Host-side check of a row table: tile_begin prefix sums, n_tiles, step
+// classes and addresses.  Returns the dtype kind the rows share (or mixed).
+int check_host_rows(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int n_classes,
+                    uint32_t* kind) {
+  int64_t tile = 0;
+  uint32_t first = rows[0].flags & 3u;
+  *kind = first;
+  for (int64_t r = 0; r < n_rows; ++r) {
+    const srs_row& row = rows[r];
+    if (row.numel < 0) return fail(SRS_ERR_INVALID_ARGUMENT, "row %lld: negative numel", (long long)r);
+    if (row.tile_begin != tile)
+      return fail(SRS_ERR_INVALID_ARGUMENT, "row %lld: tile_begin %lld, expected %lld",
+                  (long long)r, (long long)row.tile_begin, (long long)tile);
+    const uint32_t cls = (row.flags >> SRS_ROW_CLASS_SHIFT) & 0xFFu;
+    if ((int)cls >= n_classes)
+      return fail(SRS_ERR_INVALID_ARGUMENT, "row %lld: step class %u, only %d classes",
+                  (long long)r, cls, n_classes);
+    if (row.numel > 0 && (row.param == 0 || row.grad == 0 || row.state[0] == 0 ||
+                          row.state[1] == 0))
+      return fail(SRS_ERR_INVALID_ARGUMENT, "row %lld: null address", (long long)r);
+    if ((row.flags & 3u) != first) *kind = SRS_KIND_MIXED;
+    tile += (row.numel + kTile - 1) / kTile;
+  }
+  if (tile != n_tiles)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "n_tiles is %lld, the rows hold %lld tiles",
+                (long long)n_tiles, (long long)tile);
+  return SRS_OK;
+}
+
+}  // namespace
+}  // namespace srs
+
+extern "C" int srs_adamw_multi_noalloc(const srs_row* host_rows, int64_t n_rows, int64_t n_tiles,
+                                       int m_format, int m_rule, int v_format, int v_rule,
+                                       const srs_adamw_hparams* hp, const srs_rng* rng,
+                                       int grid_ctas, void* stream) {
+  g_error[0] = '\0';
+  if (!valid_format(m_format) || !valid_format(v_format))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format (%d, %d)", m_format, v_format);
+  if (!valid_rule(m_rule) || !valid_rule(v_rule))
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule (%d, %d)", m_rule, v_rule);
+  if (hp == nullptr || rng == nullptr)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null hyperparameter or rng pointer");
+  if (rng->key_mode != SRS_KEY_DERIVE && rng->key_mode != SRS_KEY_GIVEN)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown key_mode %d", rng->key_mode);
+  if (int rc = check_hp_classes(hp->n_step_classes)) return rc;
+  if (n_rows < 0 || n_tiles < 0) return fail(SRS_ERR_INVALID_ARGUMENT, "negative row/tile count");
+  if (n_rows > SRS_NOALLOC_MAX_ROWS)
+    return fail(SRS_ERR_INVALID_ARGUMENT,
+                "%lld rows exceed the fixed table of srs_adamw_multi_noalloc (at most %d rows); "
+                "split the group or use srs_adamw_multi",
+                (long long)n_rows, SRS_NOALLOC_MAX_ROWS);
+  if (n_rows == 0) {
+    if (n_tiles != 0) return fail(SRS_ERR_INVALID_ARGUMENT, "tiles given without rows");
+    return SRS_OK;
+  }
+  if (host_rows == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null row table");
+  uint32_t kind = 0;
+  if (int rc = check_host_rows(host_rows, n_rows, n_tiles, hp->n_step_classes, &kind)) return rc;
+  if (n_tiles == 0) return SRS_OK;
+  if (int rc = check_device()) return rc;
+  srs_row* table = nullptr;
+  if (int rc = noalloc_table(&table)) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Stream-ordered: the kernel below (and any later call's copy on this stream)
+  // sees exactly these rows.  From pageable memory the copy has consumed
+  // host_rows when it returns; from page-locked memory it reads them later.
+  cudaError_t e = cudaMemcpyAsync(table, host_rows, (size_t)n_rows * sizeof(srs_row),
+                                  cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "srs_adamw_multi_noalloc row copy");
+  AdamWArgs a{};
+  a.hp = *hp;
+  fill_reciprocals(*hp, a);
+  a.rng = *rng;
+  a.m_stochastic = m_rule;
+  a.v_stochastic = v_rule;
+  e = kAdamW[m_format][v_format](table, n_rows, n_tiles, kind_index(kind), a, grid_ctas, s);
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_multi_noalloc launch");
+}

@@ -87,7 +87,11 @@ _SIGNATURES = {
     "srs_sgdm_single": ([ctypes.POINTER(SrsRow), ctypes.c_int, ctypes.c_int,
                          ctypes.POINTER(SrsSgdmHparams), ctypes.c_int, _P], ctypes.c_int),
     "srs_derive_keys": ([_P, _P, ctypes.c_int64, ctypes.POINTER(SrsRng), _P], ctypes.c_int),
+    "srs_adamw_multi_noalloc": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                 ctypes.c_int, ctypes.c_int, ctypes.POINTER(SrsAdamWHparams),
+                                 ctypes.POINTER(SrsRng), ctypes.c_int, _P], ctypes.c_int),
 }
+NOALLOC_MAX_ROWS = 4096
 ABI_VERSION = 2
 
 _lock = threading.Lock()
