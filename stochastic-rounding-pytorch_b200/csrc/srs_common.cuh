@@ -65,10 +65,23 @@ __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// a*b + c rounded toward zero, per lane.
+__device__ __forceinline__ float2 fma2_rz(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+      "fma.rz.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // RN(RN(a*b) + c) per lane: the product is rounded before the addition.
 __device__ __forceinline__ float2 mul_add_rn2(float2 a, float2 b, float2 c) {
   return make_float2(__fadd_rn(__fmul_rn(a.x, b.x), c.x), __fadd_rn(__fmul_rn(a.y, b.y), c.y));
 }
+
+__device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
 
 // ---------------------------------------------------------------- hashing --
 
@@ -188,6 +201,85 @@ __device__ __forceinline__ uint32_t f16_stochastic(float x, uint32_t h) {
   return r | ((b >> 16) & 0x8000u);
 }
 
+// ------------------------------------- stochastic rounding of screened vectors --
+//
+// Fast forms of the rules above for 8-element vectors that passed a screen (no
+// NaN; for the FP16/FP8 grids every |x| < 2^63).  Vectors that fail it use the
+// per-element functions above, so results are identical either way.
+//
+// BF16: the same integer addition as bf16_stochastic; one byte permutation
+// keeps the high halves of two sums.
+//
+// FP16/FP8 grids, in FP32 arithmetic.  With U = 2^(max(e, emin) - M) the grid
+// step at |x| and N = (~h) >> 8, the reference's decision
+//   up = (h >> 8) < floor(frac * 2^24),  frac = |x|/U - floor(|x|/U),
+// is the carry of frac*2^24 + N past 2^24, so the rounded magnitude is
+// floor_U(|x| + N*U*2^-24).  Computed as
+//   a = RZ(|x| + N*U*2^-24)   (N*U*2^-24 is exact: 24-bit N, power-of-two U)
+//   b = RZ(a + U*2^23)        (U*2^23 has unit in the last place U)
+//   y = b - U*2^23            (exact)
+// Rounding toward zero never carries a sum across a multiple of U, as every
+// such multiple in range is an FP32 number, so floor_U(a) is the exact floor;
+// adding U*2^23 then keeps whole steps only.  y lies on the target grid or
+// beyond its largest finite value, so the hardware round-to-nearest conversion
+// stores it exactly (saturating for FP8, overflowing to infinity for FP16), and
+// the sign of x is put back on y.  Checked against the CPU oracle for all 2^32
+// FP32 inputs, at random hashes and at the hashes on both sides of each
+// input's threshold.
+template <int F> struct Grid;
+template <> struct Grid<SRS_FMT_F16> {
+  static constexpr int M = 10;
+  static constexpr float kMinNormal = 0x1p-14f;
+};
+template <> struct Grid<SRS_FMT_E4M3> {
+  static constexpr int M = 3;
+  static constexpr float kMinNormal = 0x1p-6f;
+};
+template <> struct Grid<SRS_FMT_E5M2> {
+  static constexpr int M = 2;
+  static constexpr float kMinNormal = 0x1p-14f;
+};
+
+// N * 2^8 for N = (~h) >> 8: the complemented top 24 hash bits, exact as a float.
+__device__ __forceinline__ float grid_noise(uint32_t counter) {
+  return __uint2float_rn(~h32(counter) & 0xFFFFFF00u);
+}
+
+// Rounded values of two screened elements (still FP32, on the target grid).
+template <int F>
+__device__ __forceinline__ float2 grid_stochastic2(float2 x, uint32_t c0, uint32_t c1) {
+  constexpr int M = Grid<F>::M;
+  constexpr float kStep = (float)(1 << (23 - M));            // U*2^23 / 2^e'
+  constexpr float kNoise = 1.0f / (float)(1ull << (32 + M));  // 2^-(32+M)
+  const float ax = fabsf(x.x), ay = fabsf(x.y);
+  const float2 s = make_float2(
+      __uint_as_float(__float_as_uint(fmaxf(ax, Grid<F>::kMinNormal)) & 0x7F800000u),
+      __uint_as_float(__float_as_uint(fmaxf(ay, Grid<F>::kMinNormal)) & 0x7F800000u));
+  const float2 n = mul2_rn(make_float2(grid_noise(c0), grid_noise(c1)), splat2(kNoise));
+  const float2 a = make_float2(__fmaf_rz(n.x, s.x, ax), __fmaf_rz(n.y, s.y, ay));
+  const float2 b = fma2_rz(s, splat2(kStep), a);
+  const float2 y = fma2_rn(s, splat2(-kStep), b);
+  return make_float2(__uint_as_float(__float_as_uint(y.x) | (__float_as_uint(x.x) & 0x80000000u)),
+                     __uint_as_float(__float_as_uint(y.y) | (__float_as_uint(x.y) & 0x80000000u)));
+}
+
+// Screens.  BF16: no NaN among the 8 (a NaN makes the sum NaN).  Grids: the
+// sum of squares is below 2^126, so no element is NaN, infinite or >= 2^63.
+__device__ __forceinline__ bool screen_bf16(const float (&x)[kVec]) {
+  const float2 s = add2_rn(add2_rn(make_float2(x[0], x[1]), make_float2(x[2], x[3])),
+                           add2_rn(make_float2(x[4], x[5]), make_float2(x[6], x[7])));
+  const float t = s.x + s.y;
+  return t == t;
+}
+
+__device__ __forceinline__ bool screen_grid(const float (&x)[kVec]) {
+  float2 s = mul2_rn(make_float2(x[0], x[1]), make_float2(x[0], x[1]));
+  s = fma2_rn(make_float2(x[2], x[3]), make_float2(x[2], x[3]), s);
+  s = fma2_rn(make_float2(x[4], x[5]), make_float2(x[4], x[5]), s);
+  s = fma2_rn(make_float2(x[6], x[7]), make_float2(x[6], x[7]), s);
+  return s.x + s.y < 0x1p126f;
+}
+
 // ------------------------------------------------- 8-element vector types --
 
 // Storage traits: bytes per element and 32-bit words per 8-element vector.
@@ -300,6 +392,74 @@ __device__ __forceinline__ void decode8(const uint32_t (&w)[kWords<F>], float (&
   }
 }
 
+// Stochastic rounding of 8 values, one element at a time (any input).
+template <int F>
+__device__ __forceinline__ void encode8_stochastic_exact(const float (&x)[kVec], uint32_t ctr0,
+                                                      uint32_t (&w)[kWords<F>]) {
+  if constexpr (F == SRS_FMT_BF16 || F == SRS_FMT_F16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t h0 = h32(ctr0 + 2 * i), h1 = h32(ctr0 + 2 * i + 1);
+      uint32_t lo, hi;
+      if constexpr (F == SRS_FMT_BF16) {
+        lo = bf16_stochastic(x[2 * i], h0);
+        hi = bf16_stochastic(x[2 * i + 1], h1);
+      } else {
+        lo = f16_stochastic(x[2 * i], h0);
+        hi = f16_stochastic(x[2 * i + 1], h1);
+      }
+      w[i] = lo | (hi << 16);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      uint32_t word = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t h = h32(ctr0 + 4 * i + k);
+        const uint32_t b = (F == SRS_FMT_E4M3) ? e4m3_stochastic(x[4 * i + k], h)
+                                               : e5m2_stochastic(x[4 * i + k], h);
+        word |= b << (8 * k);
+      }
+      w[i] = word;
+    }
+  }
+}
+
+// Stochastic rounding of 8 screened values (see the fast forms above).
+template <int F>
+__device__ __forceinline__ void encode8_stochastic_fast(const float (&x)[kVec], uint32_t ctr0,
+                                                        uint32_t (&w)[kWords<F>]) {
+  if constexpr (F == SRS_FMT_BF16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = __float_as_uint(x[2 * i]) + (h32(ctr0 + 2 * i) & 0xFFFFu);
+      const uint32_t hi = __float_as_uint(x[2 * i + 1]) + (h32(ctr0 + 2 * i + 1) & 0xFFFFu);
+      w[i] = __byte_perm(lo, hi, 0x7632u);
+    }
+  } else if constexpr (F == SRS_FMT_F16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 y = grid_stochastic2<F>(make_float2(x[2 * i], x[2 * i + 1]), ctr0 + 2 * i,
+                                           ctr0 + 2 * i + 1);
+      const __half2 hh = __float22half2_rn(y);
+      w[i] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+  } else {
+    constexpr __nv_fp8_interpretation_t kind = (F == SRS_FMT_E4M3) ? __NV_E4M3 : __NV_E5M2;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 y0 = grid_stochastic2<F>(make_float2(x[4 * i], x[4 * i + 1]),
+                                            ctr0 + 4 * i, ctr0 + 4 * i + 1);
+      const float2 y1 = grid_stochastic2<F>(make_float2(x[4 * i + 2], x[4 * i + 3]),
+                                            ctr0 + 4 * i + 2, ctr0 + 4 * i + 3);
+      const uint32_t lo = __nv_cvt_float2_to_fp8x2(y0, __NV_SATFINITE, kind);
+      const uint32_t hi = __nv_cvt_float2_to_fp8x2(y1, __NV_SATFINITE, kind);
+      w[i] = __byte_perm(lo, hi, 0x5410u);
+    }
+  }
+}
+
 // Round 8 FP32 values into storage format F.  Element j of a stochastic rule
 // uses the hash of counter `ctr0 + j` (mod 2^32).  FP32 storage is the identity.
 template <int F>
@@ -308,61 +468,33 @@ __device__ __forceinline__ void encode8(const float (&x)[kVec], uint32_t ctr0, b
   if constexpr (F == SRS_FMT_F32) {
 #pragma unroll
     for (int j = 0; j < kVec; ++j) w[j] = __float_as_uint(x[j]);
+  } else if (stochastic) {
+    const bool fast = (F == SRS_FMT_BF16) ? screen_bf16(x) : screen_grid(x);
+    if (fast) encode8_stochastic_fast<F>(x, ctr0, w);
+    else encode8_stochastic_exact<F>(x, ctr0, w);
   } else if constexpr (F == SRS_FMT_BF16 || F == SRS_FMT_F16) {
-    if (stochastic) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t h0 = h32(ctr0 + 2 * i), h1 = h32(ctr0 + 2 * i + 1);
-        uint32_t lo, hi;
-        if constexpr (F == SRS_FMT_BF16) {
-          lo = bf16_stochastic(x[2 * i], h0);
-          hi = bf16_stochastic(x[2 * i + 1], h1);
-        } else {
-          lo = f16_stochastic(x[2 * i], h0);
-          hi = f16_stochastic(x[2 * i + 1], h1);
-        }
-        w[i] = lo | (hi << 16);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = make_float2(x[2 * i], x[2 * i + 1]);
-        if constexpr (F == SRS_FMT_BF16) {
-          const __nv_bfloat162 b = __float22bfloat162_rn(f);
-          w[i] = *reinterpret_cast<const uint32_t*>(&b);
-        } else {
-          const __half2 hh = __float22half2_rn(f);
-          w[i] = *reinterpret_cast<const uint32_t*>(&hh);
-        }
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = make_float2(x[2 * i], x[2 * i + 1]);
+      if constexpr (F == SRS_FMT_BF16) {
+        const __nv_bfloat162 b = __float22bfloat162_rn(f);
+        w[i] = *reinterpret_cast<const uint32_t*>(&b);
+      } else {
+        const __half2 hh = __float22half2_rn(f);
+        w[i] = *reinterpret_cast<const uint32_t*>(&hh);
       }
     }
   } else {
-    if (stochastic) {
+    // Saturating round-to-nearest-even conversion; equal to the reference's
+    // clamp-then-grid rounding (verified exhaustively against the CPU oracle).
+    constexpr __nv_fp8_interpretation_t kind = (F == SRS_FMT_E4M3) ? __NV_E4M3 : __NV_E5M2;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        uint32_t word = 0u;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t h = h32(ctr0 + 4 * i + k);
-          const uint32_t b = (F == SRS_FMT_E4M3) ? e4m3_stochastic(x[4 * i + k], h)
-                                                 : e5m2_stochastic(x[4 * i + k], h);
-          word |= b << (8 * k);
-        }
-        w[i] = word;
-      }
-    } else {
-      // Saturating round-to-nearest-even conversion; equal to the reference's
-      // clamp-then-grid rounding (verified exhaustively against the CPU oracle).
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i], x[4 * i + 1]),
-                                                     __NV_SATFINITE,
-                                                     F == SRS_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
-        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i + 2], x[4 * i + 3]),
-                                                     __NV_SATFINITE,
-                                                     F == SRS_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
-        w[i] = (lo & 0xFFFFu) | (hi << 16);
-      }
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t lo =
+          __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i], x[4 * i + 1]), __NV_SATFINITE, kind);
+      const uint32_t hi =
+          __nv_cvt_float2_to_fp8x2(make_float2(x[4 * i + 2], x[4 * i + 3]), __NV_SATFINITE, kind);
+      w[i] = (lo & 0xFFFFu) | (hi << 16);
     }
   }
 }

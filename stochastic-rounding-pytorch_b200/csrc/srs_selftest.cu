@@ -48,7 +48,52 @@ __global__ void packed_math_kernel(uint64_t n, uint32_t seed, unsigned long long
     if (local[j]) atomicAdd(&counts[j], local[j]);
 }
 
+// Fast (screened) stochastic rounding against the per-element rules, over every
+// FP32 bit pattern: vector k holds the patterns 8k..8k+7 and uses the counter
+// base h32(k ^ seed).  counts[0] = vectors that passed the screen and were
+// compared, counts[1] = those whose encodings differ, counts[2] = screened out.
+template <int F>
+__global__ void sr_fast_kernel(uint32_t seed, unsigned long long* counts) {
+  unsigned long long local[3] = {0, 0, 0};
+  const uint64_t n_vectors = 1ull << 29;
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n_vectors;
+       k += (uint64_t)gridDim.x * blockDim.x) {
+    float x[srs::kVec];
+#pragma unroll
+    for (int j = 0; j < srs::kVec; ++j) x[j] = __uint_as_float((uint32_t)(8 * k + j));
+    const uint32_t ctr0 = srs::h32((uint32_t)k ^ seed);
+    const bool pass = (F == SRS_FMT_BF16) ? srs::screen_bf16(x) : srs::screen_grid(x);
+    if (!pass) {
+      ++local[2];
+      continue;
+    }
+    uint32_t fast[srs::kWords<F>], exact[srs::kWords<F>];
+    srs::encode8_stochastic_fast<F>(x, ctr0, fast);
+    srs::encode8_stochastic_exact<F>(x, ctr0, exact);
+    bool differ = false;
+#pragma unroll
+    for (int i = 0; i < srs::kWords<F>; ++i) differ |= fast[i] != exact[i];
+    ++local[0];
+    local[1] += differ;
+  }
+  for (int j = 0; j < 3; ++j)
+    if (local[j]) atomicAdd(&counts[j], local[j]);
+}
+
 }  // namespace
+
+extern "C" int srs_selftest_sr_fast(int format, uint32_t seed, unsigned long long* counts,
+                                    void* stream) {
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (format) {
+    case SRS_FMT_BF16: sr_fast_kernel<SRS_FMT_BF16><<<1184, 256, 0, s>>>(seed, counts); break;
+    case SRS_FMT_F16: sr_fast_kernel<SRS_FMT_F16><<<1184, 256, 0, s>>>(seed, counts); break;
+    case SRS_FMT_E4M3: sr_fast_kernel<SRS_FMT_E4M3><<<1184, 256, 0, s>>>(seed, counts); break;
+    case SRS_FMT_E5M2: sr_fast_kernel<SRS_FMT_E5M2><<<1184, 256, 0, s>>>(seed, counts); break;
+    default: return -1;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 
 extern "C" int srs_selftest_packed_math(uint64_t n, uint32_t seed, unsigned long long* counts,
                                         void* stream) {
