@@ -131,15 +131,32 @@ float exact_reciprocal(float c) {
   return best;
 }
 
-// Per step class: the exact reciprocal of bias2_sqrt and the numerator range
-// [2^-59, 2^60) of the reciprocal division (empty unless 2^-30 <= c <= 2^30).
+// Smallest float f with RN(|nss| * f) >= 2^-90 for every |m'| >= f (Inf when
+// nss is zero or not finite): products are monotone and 2^-90 is a float, so
+// |nss| * f >= 2^-90 in exact arithmetic is enough.
+float numerator_floor(float nss) {
+  const double s = std::fabs((double)nss);
+  if (!(s > 0.0) || !std::isfinite(s)) return INFINITY;
+  float f = (float)(0x1p-90 / s);
+  while (std::isfinite(f) && (double)f * s < 0x1p-90) f = std::nextafter(f, INFINITY);
+  return f;
+}
+
+// Per step class: the exact reciprocal of bias2_sqrt, the numerator range
+// [2^-59, 2^60) of the reciprocal division (empty unless 2^-30 <= c <= 2^30)
+// and whether the screened arithmetic path applies (2^-10 <= c <= 1,
+// |neg_step_size| <= 1, 0 <= eps <= 2^28; NaN scalars fail every test).
 void fill_reciprocals(const srs_adamw_hparams& hp, AdamWArgs& a) {
+  const bool eps_ok = hp.eps >= 0.0f && hp.eps <= 0x1p28f;
   for (int c = 0; c < hp.n_step_classes; ++c) {
     const float b = hp.bias2_sqrt[c];
     a.inv_bias2_sqrt[c] = exact_reciprocal(b);
     const bool ok = b >= 0x1p-30f && b <= 0x1p30f;
     a.fast_lo[c] = ok ? 0x22000000u : 0u;
     a.fast_hi[c] = ok ? 0x5D800000u : 0u;
+    const float nss = hp.neg_step_size[c];
+    a.fast_math[c] = (b >= 0x1p-10f && b <= 1.0f && nss >= -1.0f && nss <= 1.0f && eps_ok) ? 1 : 0;
+    a.m_floor[c] = numerator_floor(nss);
   }
 }
 
@@ -156,10 +173,9 @@ __global__ void derive_keys_kernel(const uint32_t* __restrict__ index, uint32_t*
 
 }  // namespace
 
-int grid_for(const void* kernel, int64_t work_ctas, int grid_ctas, cudaError_t* err) {
+int grid_for(const void* kernel, int64_t work_ctas, int grid_ctas, cudaError_t* err,
+             int smem_bytes) {
   *err = cudaSuccess;
-  if (work_ctas <= 0) return 1;
-  if (grid_ctas > 0) return (int)(work_ctas < grid_ctas ? work_ctas : grid_ctas);
   int dev = 0;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return 0;
@@ -171,12 +187,20 @@ int grid_for(const void* kernel, int64_t work_ctas, int grid_ctas, cudaError_t* 
     if (it != g_blocks_per_sm[dev].end()) per_sm = it->second;
   }
   if (per_sm == 0) {
-    *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
+    // First launch of this kernel on this device: above 48 KB a kernel must
+    // opt in to its dynamic shared memory, then the occupancy is measured.
+    if (smem_bytes > 48 * 1024) {
+      *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+      if (*err != cudaSuccess) return 0;
+    }
+    *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes);
     if (*err != cudaSuccess) return 0;
     if (per_sm < 1) per_sm = 1;
     std::lock_guard<std::mutex> lock(g_mutex);
     g_blocks_per_sm[dev][kernel] = per_sm;
   }
+  if (work_ctas <= 0) return 1;
+  if (grid_ctas > 0) return (int)(work_ctas < grid_ctas ? work_ctas : grid_ctas);
   if (sms <= 0) sms = 148;
   const int64_t full = (int64_t)sms * per_sm;
   return (int)(work_ctas < full ? work_ctas : full);

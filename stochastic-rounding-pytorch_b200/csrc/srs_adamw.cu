@@ -12,10 +12,11 @@ template <int MF, int VF, int KIND>
 static cudaError_t launch_kind(const srs_row* rows, int64_t n_rows, int64_t n_tiles,
                                const AdamWArgs& a, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
-  const int grid = grid_for(reinterpret_cast<const void*>(&adamw_kernel<MF, VF, KIND>), n_tiles,
-                            grid_ctas, &err);
+  constexpr int smem = adamw_stage_bytes<MF, VF, KIND>();
+  const void* kernel = reinterpret_cast<const void*>(&adamw_kernel<MF, VF, KIND>);
+  const int grid = grid_for(kernel, n_tiles, grid_ctas, &err, smem);
   if (err != cudaSuccess) return err;
-  adamw_kernel<MF, VF, KIND><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
+  adamw_kernel<MF, VF, KIND><<<grid, kThreads, smem, stream>>>(rows, n_rows, n_tiles, a);
   return cudaGetLastError();
 }
 

@@ -554,4 +554,22 @@ __device__ __forceinline__ void store_state8(void* base, int64_t e0, int count, 
   else store_raw_partial<F>(base, e0, count, w);
 }
 
+// store_state8 for values known to pass the screen of their format (no NaN;
+// for the FP16/FP8 grids |x| < 2^63): the stochastic rule goes straight to the
+// fast form.
+template <int F>
+__device__ __forceinline__ void store_state8_screened(void* base, int64_t e0, int count, bool vec,
+                                                      const float (&x)[kVec], uint32_t ctr0,
+                                                      bool stochastic) {
+  uint32_t w[kWords<F>];
+  if constexpr (F == SRS_FMT_F32) {
+    encode8<F>(x, ctr0, false, w);
+  } else {
+    if (stochastic) encode8_stochastic_fast<F>(x, ctr0, w);
+    else encode8<F>(x, ctr0, false, w);
+  }
+  if (vec) store_raw8<F>(base, e0, w);
+  else store_raw_partial<F>(base, e0, count, w);
+}
+
 }  // namespace srs

@@ -80,7 +80,108 @@ __global__ void sr_fast_kernel(uint32_t seed, unsigned long long* counts) {
     if (local[j]) atomicAdd(&counts[j], local[j]);
 }
 
+// The facts the screened AdamW arithmetic rests on, for every FP32 input:
+// counts[0] = inputs a >= 2^-102 whose corrected rsqrt square root differs
+// from __fsqrt_rn; counts[1] = d in [2^-126, 2^126) whose refined negated
+// reciprocal differs from -__frcp_rn(d).
+__global__ void cr_facts_kernel(unsigned long long* counts) {
+  unsigned long long bad_sqrt = 0, bad_rcp = 0;
+  for (uint32_t b = 0x00800000u + blockIdx.x * blockDim.x + threadIdx.x; b < 0x7F800000u;
+       b += gridDim.x * blockDim.x) {
+    const float a = __uint_as_float(b);
+    if (b >= 0x0C800000u) {  // 2^-102
+      const float y = srs::rsqrt_approx(a);
+      const float g = __fmul_rn(a, y), h = __fmul_rn(y, 0.5f);
+      const float s = __fmaf_rn(__fmaf_rn(-g, g, a), h, g);
+      bad_sqrt += !same(s, __fsqrt_rn(a));
+    }
+    if (b < 0x7E800000u) {  // 2^126
+      const float ny0 = srs::rcp_approx(-a);
+      const float ny1 = __fmaf_rn(__fmaf_rn(a, ny0, 1.0f), ny0, ny0);
+      bad_rcp += !same(ny1, -__frcp_rn(a));
+    }
+  }
+  if (bad_sqrt) atomicAdd(&counts[0], bad_sqrt);
+  if (bad_rcp) atomicAdd(&counts[1], bad_rcp);
+}
+
+// Screened AdamW arithmetic (adamw_update_fast) against the per-element IEEE
+// operations on random vectors whose exponents range from realistic to
+// extreme: counts[0] = vectors that passed the screen, counts[1] = vectors
+// whose parameters differ, counts[2] = vectors screened out.
+__device__ __forceinline__ float random_scaled(uint32_t h, int lo, int span, bool sign) {
+  const int e = lo + (int)((h >> 23) % (uint32_t)span);
+  const float mant = __uint_as_float(0x3F800000u | (h & 0x7FFFFFu));
+  const float x = ldexpf(mant, e);
+  return sign && (h & 0x10000u) ? -x : x;
+}
+
+__global__ void adamw_fast_kernel(uint64_t n_vectors, uint32_t seed, srs::ClassScalars k,
+                                  const __grid_constant__ srs::AdamWArgs a,
+                                  unsigned long long* counts) {
+  unsigned long long local[3] = {0, 0, 0};
+  for (uint64_t vi = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; vi < n_vectors;
+       vi += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t base = srs::h32((uint32_t)vi ^ seed);
+    const bool extreme = (base & 3u) == 0u;
+    float p[srs::kVec], m1[srs::kVec], v1[srs::kVec];
+#pragma unroll
+    for (int j = 0; j < srs::kVec; ++j) {
+      const uint32_t h0 = srs::h32(base + 3u * j), h1 = srs::h32(base + 3u * j + 1u),
+                     h2 = srs::h32(base + 3u * j + 2u);
+      p[j] = random_scaled(h0, extreme ? -140 : -20, extreme ? 270 : 22, true);
+      m1[j] = random_scaled(h1, extreme ? -110 : -30, extreme ? 180 : 32, true);
+      v1[j] = random_scaled(h2, extreme ? -100 : -50, extreme ? 150 : 55, false);
+    }
+    if (!srs::adamw_screen(m1, v1, k.m_floor)) {
+      ++local[2];
+      continue;
+    }
+    float fast[srs::kVec];
+#pragma unroll
+    for (int j = 0; j < srs::kVec; ++j) fast[j] = p[j];
+    srs::adamw_update_fast(fast, m1, v1, k, a);
+    bool differ = false;
+#pragma unroll
+    for (int j = 0; j < srs::kVec; ++j) {
+      const float root = __fsqrt_rn(v1[j]);
+      const float den = __fadd_rn(__fdiv_rn(root, k.c), a.hp.eps);
+      const float upd = __fdiv_rn(__fmul_rn(k.nss, m1[j]), den);
+      const float want = __fadd_rn(__fmul_rn(p[j], a.hp.decay), upd);
+      differ |= !same(fast[j], want);
+    }
+    ++local[0];
+    local[1] += differ;
+  }
+  for (int j = 0; j < 3; ++j)
+    if (local[j]) atomicAdd(&counts[j], local[j]);
+}
+
 }  // namespace
+
+extern "C" int srs_selftest_cr_facts(unsigned long long* counts, void* stream) {
+  cr_facts_kernel<<<1184, 256, 0, static_cast<cudaStream_t>(stream)>>>(counts);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// One step class with scalars (c, nss, eps, decay); the host-side eligibility
+// rules of the library are the caller's to respect (fast_math must hold).
+extern "C" int srs_selftest_adamw_fast(uint64_t n_vectors, uint32_t seed, float c, float inv_c,
+                                       float nss, float m_floor, float eps, float decay,
+                                       unsigned long long* counts, void* stream) {
+  srs::AdamWArgs a{};
+  a.hp.eps = eps;
+  a.hp.decay = decay;
+  srs::ClassScalars k{};
+  k.nss = nss;
+  k.c = c;
+  k.inv_c = inv_c;
+  k.fast_math = true;
+  k.m_floor = m_floor;
+  adamw_fast_kernel<<<1184, 256, 0, static_cast<cudaStream_t>(stream)>>>(n_vectors, seed, k, a,
+                                                                        counts);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 
 extern "C" int srs_selftest_sr_fast(int format, uint32_t seed, unsigned long long* counts,
                                     void* stream) {

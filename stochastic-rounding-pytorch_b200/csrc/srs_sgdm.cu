@@ -7,10 +7,11 @@ template <int UF, int KIND>
 static cudaError_t launch_kind(const srs_row* rows, int64_t n_rows, int64_t n_tiles,
                                const SgdmArgs& a, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
-  const int grid = grid_for(reinterpret_cast<const void*>(&sgdm_kernel<UF, KIND>), n_tiles,
-                            grid_ctas, &err);
+  constexpr int smem = sgdm_stage_bytes<UF, KIND>();
+  const void* kernel = reinterpret_cast<const void*>(&sgdm_kernel<UF, KIND>);
+  const int grid = grid_for(kernel, n_tiles, grid_ctas, &err, smem);
   if (err != cudaSuccess) return err;
-  sgdm_kernel<UF, KIND><<<grid, kThreads, 0, stream>>>(rows, n_rows, n_tiles, a);
+  sgdm_kernel<UF, KIND><<<grid, kThreads, smem, stream>>>(rows, n_rows, n_tiles, a);
   return cudaGetLastError();
 }
 
