@@ -18,6 +18,12 @@ against the measured copy bandwidth; e2e = the same step through the public
 optimizer API with the gradients copied in from pinned host memory and the
 updated parameters copied back every step; cpu_baseline = the CPU oracle on
 this host's cores over a bounded sample of the same workload.
+
+Other workloads of the same path (one GPU; not the headline):
+    --workload sgdm-gpt2   momentum SGD at the GPT-2-small shape (148 tensors,
+                           124,439,808 FP32 params, BF16 stochastic momentum)
+    --workload cast        the standalone cast, FP32 -> BF16/FP16/E4M3/E5M2 x
+                           {stochastic, nearest}, one line per target and rule
 """
 
 from __future__ import annotations
@@ -39,6 +45,12 @@ METRIC = "AdamW-SR step params/sec & HBM GB/s (% of peak) at 8B shape, 1/2/4/8 B
 # Algorithmic bytes per parameter: read p, g, m, v; write p, m, v
 # (BF16 p/g = 2 B, E4M3 m = 1 B, BF16 v = 2 B): 2+2+1+2 + 2+1+2 = 12.
 BYTES_PER_PARAM = 12
+# DRAM bytes per parameter of one AdamW launch measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum over the 436,228,096 parameters
+# of the 2-layer profiling case; profiles/adamw_kernel_llama3-8b-2layer.md).
+# Traffic grows in proportion to the parameters, so a full launch moves this
+# many bytes per parameter.
+MEASURED_TRAFFIC_PER_PARAM = 11.917
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -57,6 +69,10 @@ def parse_args(argv=None):
     parser.add_argument("--no-embeddings", action="store_true",
                         help="drop the two 128256x4096 matrices (profiling case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast"),
+                        default="adamw-8b")
+    parser.add_argument("--cast-elems", type=int, default=1 << 30,
+                        help="elements of the cast workload (FP32 input)")
     return parser.parse_args(argv)
 
 
@@ -202,11 +218,13 @@ def time_steps(opt, steps, world, stream):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    torch.cuda.nvtx.range_push("timed")  # profilers can select the timed steps
     start.record(stream)
     for i in range(steps):
         opt.step()
         marks[i].record(stream)
     end.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     total_ms = start.elapsed_time(end)
@@ -311,9 +329,14 @@ def run_b200(args):
                    "grad_dtype": "bf16", "exp_avg": "float8_e4m3fn stochastic",
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",
                    "global_batch": None, "seq_len": None,
-                   "l2": "56 GB of inputs per step, larger than L2; no flush"},
+                   "l2": f"{BYTES_PER_PARAM * local / 1e9:.0f} GB moved per step and GPU, "
+                         "larger than the 126 MB L2; no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
+                     "frac": achieved / peak,
+                     "traffic": MEASURED_TRAFFIC_PER_PARAM * local,
+                     "traffic_source": "ncu dram bytes per parameter of the 2-layer case, "
+                                       "scaled to this launch",
+                     "peak_source": peak_source,
                      "kernel": "srs::adamw_kernel<E4M3,BF16>", "kernel_ms": kernel_ms,
                      "bytes_per_param": BYTES_PER_PARAM, "params_per_launch": local},
         "allgather_ms": gather_ms if world > 1 else 0.0,
@@ -331,6 +354,112 @@ def run_b200(args):
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def run_sgdm_gpt2(args):
+    """Momentum SGD at the GPT-2-small shape on one GPU."""
+    import torch
+
+    from sr_states import StateFormat
+    from sr_states.distributed import ZeroSGDM
+    from sr_states.shapes import gpt2_small
+
+    peak, peak_source = measured_hbm_peak()
+    shapes = [s for _, s in gpt2_small()]
+    total = sum(math.prod(s) for s in shapes)
+    device = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=device).manual_seed(11)
+    flat_p = torch.empty(total, dtype=torch.float32, device=device).normal_(0, 0.02,
+                                                                             generator=gen)
+    flat_g = torch.empty(total, dtype=torch.float32, device=device).normal_(0, 1e-3,
+                                                                             generator=gen)
+    params, offset = [], 0
+    for shape in shapes:
+        n = math.prod(shape)
+        p = torch.nn.Parameter(flat_p[offset:offset + n].view(shape))
+        p.grad = flat_g[offset:offset + n].view(shape)
+        params.append(p)
+        offset += n
+    opt = ZeroSGDM(params, lr=1e-2, momentum=0.9,
+                   state_format={"momentum_buffer": StateFormat(torch.bfloat16, "stochastic")},
+                   seed=11)
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    opt.timings.clear()
+    stream = torch.cuda.current_stream()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        total_ms, per_step = time_steps(opt, args.steps, 1, stream)
+    ms = total_ms / args.steps
+    kernel_ms = statistics.mean(t["update_ms"] for t in opt.timings)
+    bytes_per_param = 16  # read p (4), g (4), u (2); write p (4), u (2)
+    achieved = bytes_per_param * total / (kernel_ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "SGDM-SR step params/sec & HBM GB/s at GPT-2-small shape", "value":
+        total / (ms / 1e3), "unit": "params/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "gpt2-small momentum SGD step (BASELINE config 3)",
+                   "params": total, "tensors": len(params), "param_dtype": "f32",
+                   "grad_dtype": "f32", "momentum_buffer": "bfloat16 stochastic",
+                   "l2": f"{bytes_per_param * total / 1e9:.1f} GB moved per step, larger than "
+                         "L2; no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
+                     "kernel": "srs::sgdm_kernel<BF16>", "kernel_ms": kernel_ms,
+                     "bytes_per_param": bytes_per_param},
+        "step_ms_min": min(per_step), "gpu_launches": opt.launches_per_step() * args.steps,
+        "clocks": clocks.report()}), flush=True)
+
+
+def run_cast(args):
+    """The standalone cast of FP32 data: magnitudes 2^U(-20, 18)
+    with random signs; one line per target format and rule at --cast-elems."""
+    import torch
+
+    from sr_states.cuda.cast import cast
+
+    peak, peak_source = measured_hbm_peak()
+    n = args.cast_elems
+    device = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=device).manual_seed(7)
+    x = torch.empty(n, device=device).uniform_(-20, 18, generator=gen).exp2_()
+    x *= torch.empty(n, device=device).bernoulli_(0.5, generator=gen).mul_(2).sub_(1)
+    stream = torch.cuda.current_stream()
+    for dtype, size in ((torch.bfloat16, 2), (torch.float16, 2), (torch.float8_e4m3fn, 1),
+                        (torch.float8_e5m2, 1)):
+        for rule in ("stochastic", "nearest"):
+            offset = 0
+            for _ in range(args.warmup):
+                cast(x, dtype=dtype, rounding=rule, seed=7, offset=offset)
+                offset += n
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                enable_timing=True)
+            with ClockSampler(torch.cuda.current_device()) as clocks:
+                torch.cuda.nvtx.range_push("timed")
+                start.record(stream)
+                for _ in range(args.steps):
+                    out = cast(x, dtype=dtype, rounding=rule, seed=7, offset=offset)
+                    offset += n
+                end.record(stream)
+                torch.cuda.nvtx.range_pop()
+                torch.cuda.synchronize()
+            ms = start.elapsed_time(end) / args.steps
+            achieved = (4 + size) * n / (ms / 1e3) / 1e9
+            print(json.dumps({
+                "metric": "cast elements/sec & HBM GB/s", "value": n / (ms / 1e3),
+                "unit": "elements/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"cast FP32 -> {str(dtype).split('.')[-1]} {rule} "
+                                       "(BASELINE config 2)", "elements": n},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
+                             "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                             "peak_source": peak_source, "kernel": "srs::cast_kernel",
+                             "bytes_per_elem": 4 + size},
+                "gpu_launches": args.steps, "clocks": clocks.report()}), flush=True)
+            del out
 
 
 def run_reference(args):
@@ -361,6 +490,10 @@ def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "sgdm-gpt2":
+        run_sgdm_gpt2(args)
+    elif args.workload == "cast":
+        run_cast(args)
     else:
         run_b200(args)
 

@@ -14,7 +14,7 @@ import torch
 from .._hash import split_words
 from ..rounding import native_codes
 from . import _native
-from ._tables import collect_updates, group_cache
+from ._tables import FastStep, Launch, collect_updates, current_streams, fingerprint, group_cache
 
 _F32 = np.float32
 
@@ -63,12 +63,47 @@ def _stream(device):
     return torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else None
 
 
+# A repeated step of an unchanged group (same tensors at the same addresses and
+# sizes, same formats and streams, every AdamW step advanced by one) reuses the
+# launches prepared by the last full step instead of rebuilding them from the
+# items: the row tables, layout and overlap checks of that step still hold.
+# Hyperparameters are validated on every step.
+
+
+def _fast_step(optimizer, group, formats, uses_step):
+    """(cache, key, launches, steps) for a repeated step, or (cache, key, None, None)."""
+    cache = group_cache(optimizer, group)
+    key = fingerprint(optimizer, group, formats)
+    fast = cache.fast
+    if fast is None or fast.key != key or fast.streams != current_streams(fast.launches):
+        return cache, key, None, None
+    if not uses_step:
+        return cache, key, fast.launches, None
+    steps = [state.get("step", 0) + 1 for state in fast.states]
+    if any(s != t + 1 for s, t in zip(steps, fast.steps)):
+        return cache, key, None, None
+    launches = [Launch(l.device, l.table, tuple(s + 1 for s in l.steps)) for l in fast.launches]
+    return cache, key, launches, steps
+
+
+def _remember(cache, optimizer, group, formats, launches, items, uses_step):
+    cache.fast = FastStep(fingerprint(optimizer, group, formats), current_streams(launches),
+                          launches, [item[1] for item in items] if uses_step else [],
+                          [item[3] for item in items] if uses_step else [])
+
+
 def adamw_group_step(optimizer, group, formats, items, rng_step) -> None:
-    items = list(items)
-    if not items:
-        return
-    launcher, ((m_fmt, m_rule), (v_fmt, v_rule)), launches = _prepare(
-        optimizer, group, formats, items, uses_step=True)
+    optimizer._validate_group(group)
+    codes = [native_codes(fmt.dtype, fmt.rounding) for fmt in formats]
+    cache, _, launches, steps = _fast_step(optimizer, group, formats, uses_step=True)
+    if launches is None:
+        items = list(items)
+        if not items:
+            return
+        launcher, codes, launches = _prepare(optimizer, group, formats, items, uses_step=True)
+    else:
+        launcher = _native.launcher()
+    ((m_fmt, m_rule), (v_fmt, v_rule)) = codes
     rng = rng_words(group["sr_seed"], rng_step)
     optimizer._srs_launches = getattr(optimizer, "_srs_launches", 0) + len(launches)
     for launch in launches:
@@ -77,16 +112,29 @@ def adamw_group_step(optimizer, group, formats, items, rng_step) -> None:
         with torch.cuda.device(launch.device) if launch.device.type == "cuda" else _null():
             launcher.adamw_multi(launch.table, launch.table.n_rows, launch.table.n_tiles, m_fmt,
                                  m_rule, v_fmt, v_rule, hp, rng, _stream(launch.device))
-    for _, state, _, step, _ in items:
-        state["step"] = step
+    if steps is None:
+        for _, state, _, step, _ in items:
+            state["step"] = step
+        _remember(cache, optimizer, group, formats, launches, items, True)
+    else:
+        for state, step in zip(cache.fast.states, steps):
+            state["step"] = step
+        cache.fast.launches, cache.fast.steps = launches, steps
 
 
 def sgdm_group_step(optimizer, group, formats, items, rng_step) -> None:
-    items = list(items)
-    if not items:
-        return
-    launcher, ((u_fmt, u_rule),), launches = _prepare(optimizer, group, formats, items,
-                                                      uses_step=False)
+    optimizer._validate_group(group)
+    codes = [native_codes(fmt.dtype, fmt.rounding) for fmt in formats]
+    cache, _, launches, _ = _fast_step(optimizer, group, formats, uses_step=False)
+    fresh = launches is None
+    if fresh:
+        items = list(items)
+        if not items:
+            return
+        launcher, codes, launches = _prepare(optimizer, group, formats, items, uses_step=False)
+    else:
+        launcher = _native.launcher()
+    ((u_fmt, u_rule),) = codes
     rng = rng_words(group["sr_seed"], rng_step)
     hp = sgdm_hparams(group["lr"], group["momentum"])
     optimizer._srs_launches = getattr(optimizer, "_srs_launches", 0) + len(launches)
@@ -94,6 +142,8 @@ def sgdm_group_step(optimizer, group, formats, items, rng_step) -> None:
         with torch.cuda.device(launch.device) if launch.device.type == "cuda" else _null():
             launcher.sgdm_multi(launch.table, launch.table.n_rows, launch.table.n_tiles, u_fmt,
                                 u_rule, hp, rng, _stream(launch.device))
+    if fresh:
+        _remember(cache, optimizer, group, formats, launches, items, False)
 
 
 class _null:

@@ -132,11 +132,65 @@ def _step_classes(updates):
     return [rank.get(u.step, 0) for u in updates], steps
 
 
+@dataclass
+class FastStep:
+    """What a repeated step of an unchanged group needs: the launches of the last
+    full preparation and, for AdamW, the state dicts and steps they were built for."""
+
+    key: tuple
+    streams: tuple
+    launches: list  # Launch objects; AdamW step tuples advance with every step
+    states: list  # state dict of every updated parameter (AdamW)
+    steps: list  # next step of every updated parameter at the last step (AdamW)
+
+
+def fingerprint(optimizer, group, formats) -> tuple:
+    """Identity, address and size of every tensor a step of ``group`` touches.
+
+    Two equal fingerprints mean the same parameter, gradient and state objects
+    at the same addresses and sizes, so the row tables, the layout checks and
+    the overlap check of the first of the two steps still hold."""
+    try:
+        return _fingerprint(optimizer.state, optimizer._state_names, group["params"], formats)
+    except RuntimeError:  # e.g. a sparse gradient has no data pointer: take the full path
+        return None
+
+
+def _fingerprint(state, names, params, formats) -> tuple:
+    # One flat tuple per parameter; written for the interpreter's speed, as it
+    # runs on every step (about 1 us per parameter).
+    parts = [tuple(formats)]
+    append, get = parts.append, state.get
+    n0 = names[0]
+    n1 = names[1] if len(names) > 1 else None
+    for p in params:
+        g = p.grad
+        if g is None:
+            append(None)
+            continue
+        st = get(p)
+        if st is None:
+            append((id(p), p.data_ptr(), p.numel(), id(g), g.data_ptr(), g.numel()))
+            continue
+        s0 = st.get(n0)
+        s1 = st.get(n1) if n1 is not None else None
+        append((id(p), p.data_ptr(), p.numel(), id(g), g.data_ptr(), g.numel(), id(st),
+                id(s0), s0.data_ptr() if s0 is not None else 0,
+                id(s1), s1.data_ptr() if s1 is not None else 0))
+    return tuple(parts)
+
+
+def current_streams(launches) -> tuple:
+    return tuple(torch.cuda.current_stream(launch.device) if launch.device.type == "cuda"
+                 else None for launch in launches)
+
+
 class GroupTableCache:
     """Device row tables of one parameter group, reused across steps."""
 
     def __init__(self):
         self._entries: dict[torch.device, _Entry] = {}
+        self.fast: FastStep | None = None
 
     def prepare(self, by_device, tile_elems: int) -> list[Launch]:
         entries, launches = {}, []
