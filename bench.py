@@ -8,8 +8,9 @@ A step is one optimizer step of the whole parameter set: 291 tensors,
 stochastic first moment and BF16 stochastic second moment, lr 3e-4, weight
 decay 0.1, seed 7.  With N GPUs the step is sharded ZeRO-1 style (each rank
 updates its flat shard, states exist only for it) and the updated BF16
-parameters are reassembled with an in-place NCCL all-gather, which is part
-of the timed step.  Inputs are synthetic and resident in HBM (56 GB per GPU
+parameters are reassembled on every rank inside the timed step: the fused
+kernel stores them into the peers' replicas over NVLink (an NCCL all-gather
+when peer mappings are unavailable).  Inputs are synthetic and resident in HBM (56 GB per GPU
 at N=1, far above the 126 MB L2, so no cache flush is needed).
 
 Prints one JSON line (rank 0): value = parameters updated per second by the
@@ -46,11 +47,11 @@ METRIC = "AdamW-SR step params/sec & HBM GB/s (% of peak) at 8B shape, 1/2/4/8 B
 # (BF16 p/g = 2 B, E4M3 m = 1 B, BF16 v = 2 B): 2+2+1+2 + 2+1+2 = 12.
 BYTES_PER_PARAM = 12
 # DRAM bytes per parameter of one AdamW launch measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum over the 436,228,096 parameters
-# of the 2-layer profiling case; profiles/adamw_kernel_llama3-8b-2layer.md).
+# (dram__bytes_read.sum + dram__bytes_write.sum = 5.197 GB over the 436,228,096
+# parameters of the 2-layer profiling case; profiles/adamw_kernel_llama3-8b.md).
 # Traffic grows in proportion to the parameters, so a full launch moves this
 # many bytes per parameter.
-MEASURED_TRAFFIC_PER_PARAM = 11.917
+MEASURED_TRAFFIC_PER_PARAM = 11.913
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -328,6 +329,10 @@ def run_b200(args):
                    "params": total, "tensors": len(params), "param_dtype": "bf16",
                    "grad_dtype": "bf16", "exp_avg": "float8_e4m3fn stochastic",
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",
+                   "gather": {"fused": "updated parameters stored into every peer replica by "
+                                       "the step kernel (NVLink peer stores)",
+                              "nccl": "NCCL all-gather after the step",
+                              "none": "one rank"}[opt.gather_mode],
                    "global_batch": None, "seq_len": None,
                    "l2": f"{BYTES_PER_PARAM * local / 1e9:.0f} GB moved per step and GPU, "
                          "larger than the 126 MB L2; no flush"},
@@ -339,7 +344,7 @@ def run_b200(args):
                      "peak_source": peak_source,
                      "kernel": "srs::adamw_kernel<E4M3,BF16>", "kernel_ms": kernel_ms,
                      "bytes_per_param": BYTES_PER_PARAM, "params_per_launch": local},
-        "allgather_ms": gather_ms if world > 1 else 0.0,
+        "gather_ms": gather_ms if world > 1 else 0.0,
         "step_ms_min": min(per_step), "gpu_launches": opt.launches_per_step() * args.steps,
         "clocks": clocks.report(),
     }

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define SRS_ABI_VERSION 2
+#define SRS_ABI_VERSION 3
 
 /* ---- status codes ------------------------------------------------------ */
 #define SRS_OK 0
@@ -148,6 +148,46 @@ int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_
 int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
                    int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
                    uint32_t uniform_kind, int grid_ctas, void* stream);
+
+/* ---- fused step + all-gather over peer memory ----------------------------
+ * No counterpart in the reference (it has no sharded step; this is the
+ * ZeRO-1 all-gather of the updated parameters fused into the step).  With
+ * every rank's parameters in a flat buffer of identical layout, the step
+ * stores each updated parameter vector both locally and at the same offset of
+ * every peer's buffer (plain stores through NVLink peer mappings), so no
+ * separate all-gather runs.  delta_*[w] = (peer w's buffer) - (this rank's
+ * buffer) in this process's address space, for FP32 and BF16 parameters.
+ * The caller orders the step against the peers (a barrier before, so no peer
+ * still reads its replica, and one after, before anyone uses the result).
+ */
+#define SRS_MAX_PEERS 7
+typedef struct srs_peers {
+  int32_t n_peers; /* 0..SRS_MAX_PEERS */
+  int32_t reserved;
+  int64_t delta_f32[SRS_MAX_PEERS];
+  int64_t delta_bf16[SRS_MAX_PEERS];
+} srs_peers;
+
+int srs_adamw_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
+                           int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
+                           const srs_rng* rng, uint32_t uniform_kind, const srs_peers* peers,
+                           int grid_ctas, void* stream);
+
+int srs_sgdm_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
+                          int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
+                          uint32_t uniform_kind, const srs_peers* peers, int grid_ctas,
+                          void* stream);
+
+/* Peer mappings (CUDA IPC) of the buffers above.  srs_ipc_export writes a
+ * handle of the allocation holding device address `p` (SRS_IPC_HANDLE_BYTES
+ * bytes) and the offset of `p` inside it; srs_ipc_import maps a peer's
+ * allocation into this process on the current device; srs_ipc_close unmaps
+ * it.  Allocations from the virtual-memory API (expandable segments) cannot
+ * be exported: srs_ipc_export then fails and the caller keeps a collective. */
+#define SRS_IPC_HANDLE_BYTES 64
+int srs_ipc_export(const void* p, void* handle, uint64_t* offset);
+int srs_ipc_import(const void* handle, void** base);
+int srs_ipc_close(void* base);
 
 /* ---- multi-tensor AdamW step that allocates nothing ----------------------
  * No counterpart in the reference.  Same update as srs_adamw_multi, for

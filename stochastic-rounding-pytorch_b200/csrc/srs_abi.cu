@@ -8,6 +8,8 @@
 #include <mutex>
 #include <unordered_map>
 
+#include <cuda.h>
+
 #include "srs_kernels.cuh"
 
 namespace srs {
@@ -259,9 +261,18 @@ static int check_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, con
   return SRS_OK;
 }
 
-int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
-                    int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
-                    const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream) {
+static int check_peers(const srs_peers* peers) {
+  if (peers == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null peers");
+  if (peers->n_peers < 0 || peers->n_peers > SRS_MAX_PEERS)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "n_peers must be in [0, %d], got %d", SRS_MAX_PEERS,
+                peers->n_peers);
+  return SRS_OK;
+}
+
+static int adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
+                       int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
+                       const srs_rng* rng, uint32_t uniform_kind, const srs_peers* peers,
+                       int grid_ctas, void* stream, const char* what) {
   g_error[0] = '\0';
   if (!valid_format(m_format) || !valid_format(v_format))
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format (%d, %d)", m_format, v_format);
@@ -269,6 +280,8 @@ int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule (%d, %d)", m_rule, v_rule);
   if (int rc = check_multi(rows, n_rows, n_tiles, hp, rng)) return rc;
   if (int rc = check_hp_classes(hp->n_step_classes)) return rc;
+  if (peers != nullptr)
+    if (int rc = check_peers(peers)) return rc;
   if (n_tiles == 0) return SRS_OK;
   if (int rc = check_device()) return rc;
   AdamWArgs a{};
@@ -277,29 +290,123 @@ int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_
   a.rng = *rng;
   a.m_stochastic = m_rule;
   a.v_stochastic = v_rule;
+  if (peers != nullptr) a.peers = *peers;
   const cudaError_t e = kAdamW[m_format][v_format](rows, n_rows, n_tiles,
                                                    kind_index(uniform_kind), a, grid_ctas,
                                                    static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_multi launch");
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, what);
 }
 
-int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
-                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
-                   uint32_t uniform_kind, int grid_ctas, void* stream) {
+static int sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
+                      int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
+                      uint32_t uniform_kind, const srs_peers* peers, int grid_ctas, void* stream,
+                      const char* what) {
   g_error[0] = '\0';
   if (!valid_format(u_format))
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format %d", u_format);
   if (!valid_rule(u_rule)) return fail(SRS_ERR_INVALID_ARGUMENT, "unknown rounding rule %d", u_rule);
   if (int rc = check_multi(rows, n_rows, n_tiles, hp, rng)) return rc;
+  if (peers != nullptr)
+    if (int rc = check_peers(peers)) return rc;
   if (n_tiles == 0) return SRS_OK;
   if (int rc = check_device()) return rc;
   SgdmArgs a{};
   a.hp = *hp;
   a.rng = *rng;
   a.u_stochastic = u_rule;
+  if (peers != nullptr) a.peers = *peers;
   const cudaError_t e = kSgdm[u_format](rows, n_rows, n_tiles, kind_index(uniform_kind), a,
                                         grid_ctas, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_sgdm_multi launch");
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, what);
+}
+
+int srs_adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
+                    int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
+                    const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream) {
+  return adamw_multi(rows, n_rows, n_tiles, m_format, m_rule, v_format, v_rule, hp, rng,
+                     uniform_kind, nullptr, grid_ctas, stream, "srs_adamw_multi launch");
+}
+
+int srs_adamw_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
+                           int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
+                           const srs_rng* rng, uint32_t uniform_kind, const srs_peers* peers,
+                           int grid_ctas, void* stream) {
+  if (peers == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null peers");
+  return adamw_multi(rows, n_rows, n_tiles, m_format, m_rule, v_format, v_rule, hp, rng,
+                     uniform_kind, peers, grid_ctas, stream, "srs_adamw_multi_gather launch");
+}
+
+int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
+                   int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
+                   uint32_t uniform_kind, int grid_ctas, void* stream) {
+  return sgdm_multi(rows, n_rows, n_tiles, u_format, u_rule, hp, rng, uniform_kind, nullptr,
+                    grid_ctas, stream, "srs_sgdm_multi launch");
+}
+
+int srs_sgdm_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
+                          int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
+                          uint32_t uniform_kind, const srs_peers* peers, int grid_ctas,
+                          void* stream) {
+  if (peers == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null peers");
+  return sgdm_multi(rows, n_rows, n_tiles, u_format, u_rule, hp, rng, uniform_kind, peers,
+                    grid_ctas, stream, "srs_sgdm_multi_gather launch");
+}
+
+// Base of the allocation holding a device address, through the driver's
+// cuMemGetAddressRange (looked up at run time; the runtime is linked
+// statically and the driver is loaded by it).
+static int allocation_base(const void* p, CUdeviceptr* base) {
+  using AddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddressRange fn = nullptr;
+  if (fn == nullptr) {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult status{};
+    const cudaError_t e =
+        cudaGetDriverEntryPoint("cuMemGetAddressRange", &sym, cudaEnableDefault, &status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDriverEntryPoint(cuMemGetAddressRange)");
+    if (status != cudaDriverEntryPointSuccess || sym == nullptr)
+      return fail(SRS_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+    fn = reinterpret_cast<AddressRange>(sym);
+  }
+  size_t size = 0;
+  const CUresult r = fn(base, &size, reinterpret_cast<CUdeviceptr>(p));
+  if (r != CUDA_SUCCESS)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "address %p is not in a device allocation (CUresult %d)",
+                p, (int)r);
+  return SRS_OK;
+}
+
+int srs_ipc_export(const void* p, void* handle, uint64_t* offset) {
+  g_error[0] = '\0';
+  if (p == nullptr || handle == nullptr || offset == nullptr)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = check_device()) return rc;
+  CUdeviceptr base = 0;
+  if (int rc = allocation_base(p, &base)) return rc;
+  static_assert(sizeof(cudaIpcMemHandle_t) == SRS_IPC_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (uint64_t)(reinterpret_cast<uintptr_t>(p) - (uintptr_t)base);
+  return SRS_OK;
+}
+
+int srs_ipc_import(const void* handle, void** base) {
+  g_error[0] = '\0';
+  if (handle == nullptr || base == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = check_device()) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int srs_ipc_close(void* base) {
+  g_error[0] = '\0';
+  if (base == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null pointer");
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
 }
 
 static int check_single_row(const srs_row* row, int64_t* n_tiles) {

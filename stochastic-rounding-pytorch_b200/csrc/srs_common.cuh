@@ -518,20 +518,25 @@ __device__ __forceinline__ void load_param8(const void* base, int64_t e0, int co
   }
 }
 
-// Parameter write-back: FP32 as is, BF16 round-to-nearest-even.
+// Parameter write-back: FP32 as is, BF16 round-to-nearest-even.  With peers,
+// the same bytes also go to the same offset of every peer's replica (plain
+// stores through the peer mappings: the fused all-gather of a sharded step).
 template <bool BF16>
 __device__ __forceinline__ void store_param8(void* base, int64_t e0, int count, bool vec,
-                                             const float (&x)[kVec]) {
-  if constexpr (BF16) {
-    uint32_t w[4];
-    encode8<SRS_FMT_BF16>(x, 0u, false, w);
-    if (vec) store_raw8<SRS_FMT_BF16>(base, e0, w);
-    else store_raw_partial<SRS_FMT_BF16>(base, e0, count, w);
-  } else {
-    uint32_t w[8];
-    encode8<SRS_FMT_F32>(x, 0u, false, w);
-    if (vec) store_raw8<SRS_FMT_F32>(base, e0, w);
-    else store_raw_partial<SRS_FMT_F32>(base, e0, count, w);
+                                             const float (&x)[kVec],
+                                             const srs_peers* peers = nullptr) {
+  constexpr int F = BF16 ? SRS_FMT_BF16 : SRS_FMT_F32;
+  uint32_t w[kWords<F>];
+  encode8<F>(x, 0u, false, w);
+  if (vec) store_raw8<F>(base, e0, w);
+  else store_raw_partial<F>(base, e0, count, w);
+  if (peers != nullptr) {
+    for (int i = 0; i < peers->n_peers; ++i) {
+      void* replica =
+          static_cast<char*>(base) + (BF16 ? peers->delta_bf16[i] : peers->delta_f32[i]);
+      if (vec) store_raw8<F>(replica, e0, w);
+      else store_raw_partial<F>(replica, e0, count, w);
+    }
   }
 }
 

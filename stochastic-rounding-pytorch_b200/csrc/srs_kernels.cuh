@@ -37,6 +37,7 @@ struct AdamWArgs {
   srs_rng rng;
   int32_t m_stochastic;
   int32_t v_stochastic;
+  srs_peers peers;  // replicas that receive the updated parameters (n_peers == 0: none)
 };
 
 struct SgdmArgs {
@@ -44,6 +45,7 @@ struct SgdmArgs {
   srs_sgdm_hparams hp;
   srs_rng rng;
   int32_t u_stochastic;
+  srs_peers peers;
 };
 
 // A row as held (uniformly) by one CTA while it walks that row's tiles.
@@ -383,7 +385,7 @@ __device__ __noinline__ void adamw8_exact(const RowView& rv, int64_t e0, int cou
     p[2 * i + 1] = p1.y;
   }
   const uint32_t ctr_m = (uint32_t)e0 + rv.ctr0, ctr_v = (uint32_t)e0 + rv.ctr1;
-  store_param8<PB>(rv.p, e0, count, VEC, p);
+  store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
   store_state8<MF>(rv.s0, e0, count, VEC, m, ctr_m, a.m_stochastic != 0);
   store_state8<VF>(rv.s1, e0, count, VEC, v, ctr_v, a.v_stochastic != 0);
 }
@@ -413,7 +415,7 @@ __device__ __forceinline__ void adamw8_compute(const RowView& rv, int64_t e0, in
     if (adamw_screen(m, v, k.m_floor)) {
       adamw_update_fast(p, m, v, k, a);
       const uint32_t ctr_m = (uint32_t)e0 + rv.ctr0, ctr_v = (uint32_t)e0 + rv.ctr1;
-      store_param8<PB>(rv.p, e0, count, VEC, p);
+      store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
       store_state8_screened<MF>(rv.s0, e0, count, VEC, m, ctr_m, a.m_stochastic != 0);
       store_state8_screened<VF>(rv.s1, e0, count, VEC, v, ctr_v, a.v_stochastic != 0);
       return;
@@ -535,6 +537,8 @@ __global__ void __launch_bounds__(kThreads, SRS_ADAMW_MIN_CTAS)
       }
     }
   } while (next_row(t, n_rows));
+  // Peer stores become visible to the peers before the step's closing barrier.
+  if (a.peers.n_peers > 0) __threadfence_system();
 }
 
 // ----------------------------------------------------------------- SGDM --
@@ -555,7 +559,7 @@ __device__ __forceinline__ void sgdm8_compute(const RowView& rv, int64_t e0, int
     u[2 * i] = u1.x;
     u[2 * i + 1] = u1.y;
   }
-  store_param8<PB>(rv.p, e0, count, VEC, p);
+  store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
   store_state8<UF>(rv.s0, e0, count, VEC, u, (uint32_t)e0 + rv.ctr0, a.u_stochastic != 0);
 }
 
@@ -644,6 +648,7 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
   } while (next_row(t, n_rows));
+  if (a.peers.n_peers > 0) __threadfence_system();
 }
 
 // ----------------------------------------------------------------- cast --

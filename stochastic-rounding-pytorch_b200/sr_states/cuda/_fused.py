@@ -59,6 +59,12 @@ def _prepare(optimizer, group, formats, items, *, uses_step):
     return launcher, codes, launches
 
 
+def _peers_of(optimizer) -> dict:
+    """Peer replicas of a sharded optimizer that fuses its all-gather into the step."""
+    peers = getattr(optimizer, "_srs_peers", None)
+    return {"peers": peers} if peers is not None else {}
+
+
 def _stream(device):
     return torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else None
 
@@ -111,7 +117,8 @@ def adamw_group_step(optimizer, group, formats, items, rng_step) -> None:
                            launch.steps)
         with torch.cuda.device(launch.device) if launch.device.type == "cuda" else _null():
             launcher.adamw_multi(launch.table, launch.table.n_rows, launch.table.n_tiles, m_fmt,
-                                 m_rule, v_fmt, v_rule, hp, rng, _stream(launch.device))
+                                 m_rule, v_fmt, v_rule, hp, rng, _stream(launch.device),
+                                 **_peers_of(optimizer))
     if steps is None:
         for _, state, _, step, _ in items:
             state["step"] = step
@@ -141,7 +148,8 @@ def sgdm_group_step(optimizer, group, formats, items, rng_step) -> None:
     for launch in launches:
         with torch.cuda.device(launch.device) if launch.device.type == "cuda" else _null():
             launcher.sgdm_multi(launch.table, launch.table.n_rows, launch.table.n_tiles, u_fmt,
-                                u_rule, hp, rng, _stream(launch.device))
+                                u_rule, hp, rng, _stream(launch.device),
+                                **_peers_of(optimizer))
     if fresh:
         _remember(cache, optimizer, group, formats, launches, items, False)
 

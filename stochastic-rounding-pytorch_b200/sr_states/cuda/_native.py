@@ -66,6 +66,16 @@ class SrsSgdmHparams(ctypes.Structure):
     _fields_ = [("momentum", ctypes.c_float), ("neg_lr", ctypes.c_float)]
 
 
+MAX_PEERS = 7
+IPC_HANDLE_BYTES = 64
+
+
+class SrsPeers(ctypes.Structure):
+    _fields_ = [("n_peers", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("delta_f32", ctypes.c_int64 * MAX_PEERS),
+                ("delta_bf16", ctypes.c_int64 * MAX_PEERS)]
+
+
 _P = ctypes.c_void_p
 _SIGNATURES = {
     "srs_abi_version": ([], ctypes.c_int),
@@ -90,9 +100,20 @@ _SIGNATURES = {
     "srs_adamw_multi_noalloc": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                  ctypes.c_int, ctypes.c_int, ctypes.POINTER(SrsAdamWHparams),
                                  ctypes.POINTER(SrsRng), ctypes.c_int, _P], ctypes.c_int),
+    "srs_adamw_multi_gather": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_int, ctypes.c_int, ctypes.POINTER(SrsAdamWHparams),
+                                ctypes.POINTER(SrsRng), ctypes.c_uint32,
+                                ctypes.POINTER(SrsPeers), ctypes.c_int, _P], ctypes.c_int),
+    "srs_sgdm_multi_gather": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                               ctypes.POINTER(SrsSgdmHparams), ctypes.POINTER(SrsRng),
+                               ctypes.c_uint32, ctypes.POINTER(SrsPeers), ctypes.c_int, _P],
+                              ctypes.c_int),
+    "srs_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "srs_ipc_import": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "srs_ipc_close": ([_P], ctypes.c_int),
 }
 NOALLOC_MAX_ROWS = 4096
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lock = threading.Lock()
 _library = None
@@ -159,15 +180,46 @@ class NativeLauncher:
                                        stream))
 
     def adamw_multi(self, table, n_rows, n_tiles, m_fmt, m_rule, v_fmt, v_rule, hp, rng, stream,
-                    grid_ctas=0):
-        _check(load_library().srs_adamw_multi(table.device_ptr, n_rows, n_tiles, m_fmt, m_rule,
+                    grid_ctas=0, peers=None):
+        lib = load_library()
+        if peers is None:
+            _check(lib.srs_adamw_multi(table.device_ptr, n_rows, n_tiles, m_fmt, m_rule, v_fmt,
+                                       v_rule, ctypes.byref(hp), ctypes.byref(rng),
+                                       table.uniform_kind, grid_ctas, stream))
+        else:
+            _check(lib.srs_adamw_multi_gather(table.device_ptr, n_rows, n_tiles, m_fmt, m_rule,
                                               v_fmt, v_rule, ctypes.byref(hp), ctypes.byref(rng),
-                                              table.uniform_kind, grid_ctas, stream))
+                                              table.uniform_kind, ctypes.byref(peers), grid_ctas,
+                                              stream))
 
-    def sgdm_multi(self, table, n_rows, n_tiles, u_fmt, u_rule, hp, rng, stream, grid_ctas=0):
-        _check(load_library().srs_sgdm_multi(table.device_ptr, n_rows, n_tiles, u_fmt, u_rule,
+    def sgdm_multi(self, table, n_rows, n_tiles, u_fmt, u_rule, hp, rng, stream, grid_ctas=0,
+                   peers=None):
+        lib = load_library()
+        if peers is None:
+            _check(lib.srs_sgdm_multi(table.device_ptr, n_rows, n_tiles, u_fmt, u_rule,
+                                      ctypes.byref(hp), ctypes.byref(rng), table.uniform_kind,
+                                      grid_ctas, stream))
+        else:
+            _check(lib.srs_sgdm_multi_gather(table.device_ptr, n_rows, n_tiles, u_fmt, u_rule,
                                              ctypes.byref(hp), ctypes.byref(rng),
-                                             table.uniform_kind, grid_ctas, stream))
+                                             table.uniform_kind, ctypes.byref(peers), grid_ctas,
+                                             stream))
+
+    def ipc_export(self, ptr):
+        """(handle bytes, offset of ptr in its allocation) for mapping in a peer process."""
+        handle = (ctypes.c_char * IPC_HANDLE_BYTES)()
+        offset = ctypes.c_uint64()
+        _check(load_library().srs_ipc_export(ptr, handle, ctypes.byref(offset)))
+        return bytes(handle), int(offset.value)
+
+    def ipc_import(self, handle: bytes) -> int:
+        base = ctypes.c_void_p()
+        buf = (ctypes.c_char * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        _check(load_library().srs_ipc_import(buf, ctypes.byref(base)))
+        return int(base.value)
+
+    def ipc_close(self, base: int) -> None:
+        _check(load_library().srs_ipc_close(base))
 
     def adamw_single(self, row, m_fmt, m_rule, v_fmt, v_rule, hp, stream, grid_ctas=0):
         _check(load_library().srs_adamw_single(ctypes.byref(row), m_fmt, m_rule, v_fmt, v_rule,

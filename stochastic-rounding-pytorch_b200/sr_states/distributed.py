@@ -7,8 +7,19 @@ of the shard with a parameter becomes one row of the fused step, with the
 parameter's global index and, as RNG offset, the index of the row's first
 element within that parameter.  The counter-hash RNG therefore gives exactly
 the bytes of an unsharded step, whatever the world size.  Optimizer states
-exist only for the local shard.  After the update each flat buffer is
-reassembled with one in-place NCCL all-gather over NVLink.
+exist only for the local shard.
+
+The updated parameters are then reassembled on every rank.  By default
+(``gather="fused"``) this happens inside the step: at construction every rank
+maps its peers' flat buffers into its address space (CUDA IPC through
+libsrs_b200.so), and the fused kernel stores each updated parameter vector
+both locally and at the same offset of every peer's buffer, so the exchange
+over NVLink overlaps the arithmetic and no separate all-gather runs.  A step
+is then: barrier (no peer still reads its replica), fused launch, barrier
+(every replica complete), each barrier a one-element NCCL all-reduce on the
+current stream.  If any rank cannot export its buffers (for example memory
+from the virtual-memory allocator), all ranks fall back to one in-place NCCL
+all-gather per flat buffer after the update (``gather="nccl"`` selects it).
 
 Gradients must be complete on every rank (already all-reduced), as in ZeRO-1.
 ``state_dict()`` holds each rank's shard of the states.
@@ -102,7 +113,9 @@ class FlatLayout:
 class _ZeroMixin:
     """ZeRO-1 behaviour for a fused StateOptimizer subclass (see module docstring)."""
 
-    def __init__(self, params, *args, process_group=None, **kwargs):
+    def __init__(self, params, *args, process_group=None, gather="fused", **kwargs):
+        if gather not in ("fused", "nccl"):
+            raise ValueError(f"gather must be 'fused' or 'nccl', got {gather!r}")
         super().__init__(params, *args, **kwargs)
         self._group = process_group
         initialized = torch.distributed.is_available() and torch.distributed.is_initialized()
@@ -112,6 +125,77 @@ class _ZeroMixin:
         self._layout = FlatLayout(ordered, self._world, self._rank)
         self._events: list = []
         self._timed: list = []
+        self._peer_bases: list[int] = []
+        self._srs_peers = None
+        self._sync = None
+        if self._world > 1:
+            device = next(iter(self._layout.buffers.values())).device
+            self._sync = torch.zeros(1, device=device)
+            if gather == "fused":
+                self._srs_peers = self._connect_peers()
+
+    @property
+    def gather_mode(self) -> str:
+        """'fused' (peer stores inside the step), 'nccl' (all-gather) or 'none' (one rank)."""
+        if self._world == 1:
+            return "none"
+        return "fused" if self._srs_peers is not None else "nccl"
+
+    def _agree(self, value):
+        """Every rank's ``value`` (a collective: all ranks call it together)."""
+        everyone = [None] * self._world
+        torch.distributed.all_gather_object(everyone, value, group=self._group)
+        return everyone
+
+    def _connect_peers(self):
+        """Map every peer's flat buffers into this process; None on every rank if
+        any rank cannot (then the step ends with an NCCL all-gather)."""
+        from .cuda import _native
+
+        buffers = self._layout.buffers
+        mine = None
+        if (self._world - 1 <= _native.MAX_PEERS
+                and all(d in (torch.float32, torch.bfloat16) for d in buffers)
+                and all(b.device.type == "cuda" for b in buffers.values())):
+            launcher = _native.launcher()
+            try:
+                mine = {str(d): launcher.ipc_export(b.data_ptr()) for d, b in buffers.items()}
+            except (ValueError, RuntimeError):
+                mine = None
+        everyone = self._agree(mine)
+        if any(entry is None for entry in everyone):
+            return None
+        peers, ok = _native.SrsPeers(), True
+        try:
+            n = 0
+            for r in range(self._world):
+                if r == self._rank:
+                    continue
+                for dtype, buf in buffers.items():
+                    handle, offset = everyone[r][str(dtype)]
+                    base = launcher.ipc_import(handle)
+                    self._peer_bases.append(base)
+                    deltas = peers.delta_bf16 if dtype == torch.bfloat16 else peers.delta_f32
+                    deltas[n] = base + offset - buf.data_ptr()
+                n += 1
+            peers.n_peers = n
+        except (ValueError, RuntimeError):
+            ok = False
+        if not all(self._agree(ok)):
+            self._close_peers()
+            return None
+        return peers
+
+    def _close_peers(self):
+        if self._peer_bases:
+            from .cuda import _native
+
+            for base in self._peer_bases:
+                _native.launcher().ipc_close(base)
+        self._peer_bases = []
+
+    def _barrier(self):
+        torch.distributed.all_reduce(self._sync, group=self._group)
 
     def local_numel(self) -> int:
         total = 0
@@ -150,36 +234,50 @@ class _ZeroMixin:
     @torch.no_grad()
     def step(self, closure=None):
         stream = torch.cuda.current_stream() if torch.cuda.is_available() else None
-        marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if stream else None
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if stream else None
+        fused = self._srs_peers is not None
         if marks:
             marks[0].record(stream)
+        if fused:
+            self._barrier()
+        if marks:
+            marks[1].record(stream)
         self._srs_launches = 0
         loss = super().step(closure)
         self._srs_launches_last_step = self._srs_launches
         if marks:
-            marks[1].record(stream)
-        if self._world > 1:
+            marks[2].record(stream)
+        if fused:
+            self._barrier()
+        elif self._world > 1:
             for dtype, buffer in self._layout.buffers.items():
                 lo, hi = self._layout.shard(dtype)
                 torch.distributed.all_gather_into_tensor(buffer, buffer[lo:hi], group=self._group)
         if marks:
-            marks[2].record(stream)
+            marks[3].record(stream)
             self._events.append(marks)
         return loss
 
     @property
     def timings(self):
-        """Per step since the last clear: update_ms (fused kernel launches) and
-        gather_ms (all-gather); reading it synchronizes on the recorded events."""
+        """Per step since the last clear: update_ms (the fused launches, including
+        their peer stores when the gather is fused) and gather_ms (the barriers
+        around a fused step, or the NCCL all-gather); reading it synchronizes on
+        the recorded events."""
         for marks in self._events:
-            marks[2].synchronize()
-            self._timed.append({"update_ms": marks[0].elapsed_time(marks[1]),
-                                "gather_ms": marks[1].elapsed_time(marks[2])})
+            marks[3].synchronize()
+            self._timed.append({"update_ms": marks[1].elapsed_time(marks[2]),
+                                "gather_ms": marks[0].elapsed_time(marks[1])
+                                + marks[2].elapsed_time(marks[3])})
         self._events = []
         return _TimingList(self._timed)
 
     def close(self):
+        """Drop recorded timings and unmap the peers' buffers (call after the last
+        step, on every rank, while the process group still exists)."""
         self._events, self._timed = [], []
+        self._close_peers()
+        self._srs_peers = None
 
 
 class _TimingList(list):
