@@ -22,7 +22,14 @@ from the virtual-memory allocator), all ranks fall back to one in-place NCCL
 all-gather per flat buffer after the update (``gather="nccl"`` selects it).
 
 Gradients must be complete on every rank (already all-reduced), as in ZeRO-1.
-``state_dict()`` holds each rank's shard of the states.
+
+Checkpoints: ``state_dict()`` gathers the shards into the unsharded layout of
+AdamWReferenceSR / SGDMReferenceSR (every state in its parameter's shape), so
+a checkpoint resumes at any world size or in the unsharded optimizer, and
+``load_state_dict`` accepts that layout and keeps the local runs.  Both are
+collectives.  ``sharded_state_dict()`` / ``load_sharded_state_dict()`` save and
+restore each rank's own runs without communication (same world size and
+parameters required).
 """
 
 from __future__ import annotations
@@ -196,6 +203,96 @@ class _ZeroMixin:
 
     def _barrier(self):
         torch.distributed.all_reduce(self._sync, group=self._group)
+
+    # ---------------------------------------------------------- checkpoints --
+
+    def _ordered_params(self):
+        return [p for g in self.param_groups for p in g["params"]]
+
+    def state_dict(self):
+        """The unsharded state dict (the layout of the unsharded optimizer),
+        assembled from every rank's runs.  A collective: call it on every rank."""
+        local = super().state_dict()
+        params = self._ordered_params()
+        if self._world == 1 and not any(
+                n in st for st in self.state.values() for n in self._state_names):
+            return local
+        device = next(iter(self._layout.buffers.values())).device
+        # Which parameters have states anywhere, and their steps.
+        present = torch.zeros(len(params), dtype=torch.int64, device=device)
+        steps = torch.zeros(len(params), dtype=torch.int64, device=device)
+        for i, p in enumerate(params):
+            st = self.state.get(p, {})
+            if self._state_names[0] in st:
+                present[i] = 1
+                steps[i] = int(st.get("step", 0))
+        if self._world > 1:
+            torch.distributed.all_reduce(present, op=torch.distributed.ReduceOp.MAX,
+                                         group=self._group)
+            torch.distributed.all_reduce(steps, op=torch.distributed.ReduceOp.MAX,
+                                         group=self._group)
+        state = {}
+        for i, p in enumerate(params):
+            if not present[i]:
+                continue
+            run = self._layout.local_run(p)
+            st = self.state.get(p, {})
+            entry = {}
+            for group in self.param_groups:
+                if any(q is p for q in group["params"]):
+                    formats = self._formats(group)
+                    break
+            for name, fmt in zip(self._state_names, formats):
+                full = torch.zeros(p.numel(), dtype=fmt.dtype, device=p.device)
+                if run is not None and name in st:
+                    full[run[0]:run[1]].copy_(st[name])
+                if self._world > 1:
+                    # Each element is non-zero on at most one rank: summing the
+                    # bytes assembles the state exactly, whatever its dtype.
+                    torch.distributed.all_reduce(full.view(torch.uint8), group=self._group)
+                entry[name] = full.view(p.shape)
+            if self._uses_step:
+                entry["step"] = int(steps[i])
+            state[i] = entry
+        local["state"] = state
+        return local
+
+    def load_state_dict(self, state_dict):
+        """Load the unsharded layout (from ``state_dict()`` here or from the
+        unsharded optimizer) and keep this rank's runs."""
+        super().load_state_dict(state_dict)
+        self._keep_local_runs()
+
+    def _keep_local_runs(self):
+        for p in self._ordered_params():
+            st = self.state.get(p)
+            if not st:
+                continue
+            run = self._layout.local_run(p)
+            if run is None:
+                del self.state[p]
+                continue
+            for name in self._state_names:
+                if name in st and st[name].numel() == p.numel():
+                    st[name] = st[name].reshape(-1)[run[0]:run[1]].clone()
+
+    def sharded_state_dict(self):
+        """This rank's runs of the states plus the layout they belong to."""
+        return {"zero1": {"world": self._world, "rank": self._rank,
+                          "numels": [p.numel() for p in self._ordered_params()]},
+                "optimizer": super().state_dict()}
+
+    def load_sharded_state_dict(self, sharded):
+        """Restore this rank's runs saved by ``sharded_state_dict()`` on the same
+        rank of a run with the same world size and parameters."""
+        meta = sharded["zero1"]
+        if (meta["world"], meta["rank"]) != (self._world, self._rank):
+            raise ValueError(
+                f"sharded checkpoint of rank {meta['rank']} of {meta['world']} cannot be "
+                f"loaded on rank {self._rank} of {self._world}; use state_dict() instead")
+        if meta["numels"] != [p.numel() for p in self._ordered_params()]:
+            raise ValueError("sharded checkpoint parameters do not match this optimizer")
+        super().load_state_dict(sharded["optimizer"])
 
     def local_numel(self) -> int:
         total = 0

@@ -103,3 +103,81 @@ def test_zero1_sharded_steps_equal_unsharded(world):
         if p.is_alive():
             p.kill()
     assert results == {r: "ok" for r in range(world)}, results
+
+
+def _checkpoint_worker(rank, world, port, queue):
+    sys.path[:0] = [str(ROOT), str(ROOT / "stochastic-rounding-pytorch_b200"), str(ROOT / "tests")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    from _support import FakeLauncher
+    from sr_states import AdamWReferenceSR
+    from sr_states.cuda import _native
+    from sr_states.distributed import ZeroAdamW
+
+    def resume(cls, checkpoint, values, grads, fmt, sharded=False):
+        params = [torch.nn.Parameter(v.clone()) for v in values]
+        opt = cls([{"params": params[:3]}, {"params": params[3:], "weight_decay": 0.0}],
+                  lr=1e-2, state_format=fmt, seed=2**40 + 3)
+        if sharded:
+            opt.load_sharded_state_dict(checkpoint)
+        else:
+            opt.load_state_dict(checkpoint)
+        for step_grads in grads:
+            for p, g in zip(params, step_grads):
+                p.grad = None if g is None else g.clone()
+            opt.step()
+        return params
+
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        _native.set_launcher(FakeLauncher())
+        params, grads, fmt = _problem()
+        reference = [torch.nn.Parameter(p.detach().clone()) for p in params]
+        ref_opt = _run(AdamWReferenceSR, reference, grads[:2], fmt)
+        sharded = _run(ZeroAdamW, params, grads[:2], fmt)
+        full = sharded.state_dict()
+        expected = ref_opt.state_dict()
+        assert set(full["state"]) == set(expected["state"])
+        for key, entry in expected["state"].items():
+            mine = full["state"][key]
+            assert mine["step"] == entry["step"]
+            for name in ("exp_avg", "exp_avg_sq"):
+                assert mine[name].shape == entry[name].shape and mine[name].dtype == entry[name].dtype
+                assert torch.equal(mine[name].view(torch.uint8), entry[name].view(torch.uint8))
+        assert full["param_groups"] == expected["param_groups"]
+        values = [p.detach().clone() for p in reference]
+        tail = grads[2:] + grads[:1]
+        ref_tail = resume(AdamWReferenceSR, expected, values, tail, fmt)
+        for cls, ckpt, kw in ((ZeroAdamW, full, {}), (AdamWReferenceSR, full, {}),
+                              (ZeroAdamW, sharded.sharded_state_dict(), {"sharded": True})):
+            got = resume(cls, ckpt, values, tail, fmt, **kw)
+            for p, q in zip(got, ref_tail):
+                assert torch.equal(p.detach().view(torch.uint8), q.detach().view(torch.uint8)), cls
+        queue.put((rank, "ok"))
+    except BaseException as exc:  # report, never hang the parent
+        import traceback
+        queue.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_zero1_checkpoints_gather_to_the_unsharded_layout_and_resume(world):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_checkpoint_worker, args=(r, world, port, queue))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results == {r: "ok" for r in range(world)}, results
