@@ -241,13 +241,14 @@ template <> struct Grid<SRS_FMT_E5M2> {
 };
 
 // N * 2^8 for N = (~h) >> 8: the complemented top 24 hash bits, exact as a float.
-__device__ __forceinline__ float grid_noise(uint32_t counter) {
-  return __uint2float_rn(~h32(counter) & 0xFFFFFF00u);
+__device__ __forceinline__ float grid_noise(uint32_t h) {
+  return __uint2float_rn(~h & 0xFFFFFF00u);
 }
 
-// Rounded values of two screened elements (still FP32, on the target grid).
+// Rounded values of two screened elements with hashes h0, h1 (still FP32, on
+// the target grid).
 template <int F>
-__device__ __forceinline__ float2 grid_stochastic2(float2 x, uint32_t c0, uint32_t c1) {
+__device__ __forceinline__ float2 grid_stochastic2(float2 x, uint32_t h0, uint32_t h1) {
   constexpr int M = Grid<F>::M;
   constexpr float kStep = (float)(1 << (23 - M));            // U*2^23 / 2^e'
   constexpr float kNoise = 1.0f / (float)(1ull << (32 + M));  // 2^-(32+M)
@@ -255,7 +256,7 @@ __device__ __forceinline__ float2 grid_stochastic2(float2 x, uint32_t c0, uint32
   const float2 s = make_float2(
       __uint_as_float(__float_as_uint(fmaxf(ax, Grid<F>::kMinNormal)) & 0x7F800000u),
       __uint_as_float(__float_as_uint(fmaxf(ay, Grid<F>::kMinNormal)) & 0x7F800000u));
-  const float2 n = mul2_rn(make_float2(grid_noise(c0), grid_noise(c1)), splat2(kNoise));
+  const float2 n = mul2_rn(make_float2(grid_noise(h0), grid_noise(h1)), splat2(kNoise));
   const float2 a = make_float2(__fmaf_rz(n.x, s.x, ax), __fmaf_rz(n.y, s.y, ay));
   const float2 b = fma2_rz(s, splat2(kStep), a);
   const float2 y = fma2_rn(s, splat2(-kStep), b);
@@ -426,22 +427,40 @@ __device__ __forceinline__ void encode8_stochastic_exact(const float (&x)[kVec],
   }
 }
 
-// Stochastic rounding of 8 screened values (see the fast forms above).
-template <int F>
-__device__ __forceinline__ void encode8_stochastic_fast(const float (&x)[kVec], uint32_t ctr0,
-                                                        uint32_t (&w)[kWords<F>]) {
+// h32 of counter c + j, one of a vector's 8 consecutive counters.  SHARED: the
+// 8 counters do not carry across bit 16, so (c + j) >> 16 == hi for all of
+// them and the first xor-shift of h32 reuses that one shift.
+template <bool SHARED>
+__device__ __forceinline__ uint32_t h32_at(uint32_t c, uint32_t j, uint32_t hi) {
+  if constexpr (SHARED) {
+    uint32_t x = (c + j) ^ hi;
+    x *= 0x7FEB352Du;
+    x ^= x >> 15;
+    x *= 0x846CA68Bu;
+    return x ^ (x >> 16);
+  } else {
+    return h32(c + j);
+  }
+}
+
+template <int F, bool SHARED>
+__device__ __forceinline__ void encode8_stochastic_fast_as(const float (&x)[kVec], uint32_t ctr0,
+                                                           uint32_t hi,
+                                                           uint32_t (&w)[kWords<F>]) {
   if constexpr (F == SRS_FMT_BF16) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t lo = __float_as_uint(x[2 * i]) + (h32(ctr0 + 2 * i) & 0xFFFFu);
-      const uint32_t hi = __float_as_uint(x[2 * i + 1]) + (h32(ctr0 + 2 * i + 1) & 0xFFFFu);
-      w[i] = __byte_perm(lo, hi, 0x7632u);
+      const uint32_t lo = __float_as_uint(x[2 * i]) + (h32_at<SHARED>(ctr0, 2 * i, hi) & 0xFFFFu);
+      const uint32_t up =
+          __float_as_uint(x[2 * i + 1]) + (h32_at<SHARED>(ctr0, 2 * i + 1, hi) & 0xFFFFu);
+      w[i] = __byte_perm(lo, up, 0x7632u);
     }
   } else if constexpr (F == SRS_FMT_F16) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 y = grid_stochastic2<F>(make_float2(x[2 * i], x[2 * i + 1]), ctr0 + 2 * i,
-                                           ctr0 + 2 * i + 1);
+      const float2 y = grid_stochastic2<F>(make_float2(x[2 * i], x[2 * i + 1]),
+                                           h32_at<SHARED>(ctr0, 2 * i, hi),
+                                           h32_at<SHARED>(ctr0, 2 * i + 1, hi));
       const __half2 hh = __float22half2_rn(y);
       w[i] = *reinterpret_cast<const uint32_t*>(&hh);
     }
@@ -450,14 +469,24 @@ __device__ __forceinline__ void encode8_stochastic_fast(const float (&x)[kVec], 
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const float2 y0 = grid_stochastic2<F>(make_float2(x[4 * i], x[4 * i + 1]),
-                                            ctr0 + 4 * i, ctr0 + 4 * i + 1);
+                                            h32_at<SHARED>(ctr0, 4 * i, hi),
+                                            h32_at<SHARED>(ctr0, 4 * i + 1, hi));
       const float2 y1 = grid_stochastic2<F>(make_float2(x[4 * i + 2], x[4 * i + 3]),
-                                            ctr0 + 4 * i + 2, ctr0 + 4 * i + 3);
+                                            h32_at<SHARED>(ctr0, 4 * i + 2, hi),
+                                            h32_at<SHARED>(ctr0, 4 * i + 3, hi));
       const uint32_t lo = __nv_cvt_float2_to_fp8x2(y0, __NV_SATFINITE, kind);
-      const uint32_t hi = __nv_cvt_float2_to_fp8x2(y1, __NV_SATFINITE, kind);
-      w[i] = __byte_perm(lo, hi, 0x5410u);
+      const uint32_t up = __nv_cvt_float2_to_fp8x2(y1, __NV_SATFINITE, kind);
+      w[i] = __byte_perm(lo, up, 0x5410u);
     }
   }
+}
+
+// Stochastic rounding of 8 screened values (see the fast forms above).
+template <int F>
+__device__ __forceinline__ void encode8_stochastic_fast(const float (&x)[kVec], uint32_t ctr0,
+                                                        uint32_t (&w)[kWords<F>]) {
+  if ((ctr0 & 0xFFFFu) <= 0xFFF8u) encode8_stochastic_fast_as<F, true>(x, ctr0, ctr0 >> 16, w);
+  else encode8_stochastic_fast_as<F, false>(x, ctr0, 0u, w);
 }
 
 // Round 8 FP32 values into storage format F.  Element j of a stochastic rule
