@@ -72,6 +72,8 @@ def parse_args(argv=None):
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast"),
                         default="adamw-8b")
+    parser.add_argument("--gather", choices=("fused", "nccl"), default="fused",
+                        help="how the sharded step reassembles the parameters at N>1")
     parser.add_argument("--cast-elems", type=int, default=1 << 30,
                         help="elements of the cast workload (FP32 input)")
     return parser.parse_args(argv)
@@ -177,7 +179,7 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload --
 
-def build_workload(world, rank, layers=32, embeddings=True):
+def build_workload(world, rank, layers=32, embeddings=True, gather="fused"):
     """Flat BF16 parameter and gradient buffers holding the 291 tensors; the
     optimizer (ZeRO-1 when world > 1) over views of them."""
     import torch
@@ -206,7 +208,7 @@ def build_workload(world, rank, layers=32, embeddings=True):
     fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn, "stochastic"),
            "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
     opt = ZeroAdamW(params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1,
-                    state_format=fmt, seed=7)
+                    state_format=fmt, seed=7, gather=gather)
     return opt, params, flat_p, flat_g, total
 
 
@@ -303,7 +305,7 @@ def run_b200(args):
     world, rank = init_distributed(args.gpus)
     peak, peak_source = measured_hbm_peak()
     opt, params, flat_p, flat_g, total = build_workload(world, rank, args.layers,
-                                                        not args.no_embeddings)
+                                                        not args.no_embeddings, args.gather)
     local = opt.local_numel()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):

@@ -8,10 +8,11 @@ cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int s
                         int vec_ok, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
   const int64_t work = (n + kTile - 1) / kTile;
+  constexpr int smem = kStages * kCastStageBytes;
   const int grid =
-      grid_for(reinterpret_cast<const void*>(&cast_kernel<OF>), work, grid_ctas, &err);
+      grid_for(reinterpret_cast<const void*>(&cast_kernel<OF>), work, grid_ctas, &err, smem);
   if (err != cudaSuccess) return err;
-  cast_kernel<OF><<<grid, kThreads, 0, stream>>>(x, y, n, base, stochastic, vec_ok);
+  cast_kernel<OF><<<grid, kThreads, smem, stream>>>(x, y, n, base, stochastic, vec_ok);
   return cudaGetLastError();
 }
 

@@ -654,17 +654,64 @@ __global__ void __launch_bounds__(kThreads)
 // ----------------------------------------------------------------- cast --
 
 // y[e] = round(x[e]); stochastic counter (e + base) mod 2^32 with base = seed + offset.
+// Round to nearest is a plain copy-like stream: a grid-stride loop of 8-element
+// vectors reaches the copy bandwidth.  The stochastic rules do more arithmetic
+// per byte: each CTA takes a contiguous range of 2048-element tiles and, with
+// aligned input and output (vec_ok), double-buffers full tiles through shared
+// memory by per-thread cp.async copies of the thread's 32 input bytes, so the
+// loads of the next tile are in flight during the hashing and rounding.
+constexpr int kCastStageBytes = kThreads * kVec * 4;  // one tile of FP32 input
+
 template <int OF>
 __global__ void __launch_bounds__(kThreads)
     cast_kernel(const float* __restrict__ x, void* __restrict__ y, int64_t n, uint32_t base,
                 int stochastic, int vec_ok) {
-  const int64_t stride = (int64_t)gridDim.x * kThreads * kVec;
-  for (int64_t e0 = ((int64_t)blockIdx.x * kThreads + threadIdx.x) * kVec; e0 < n; e0 += stride) {
-    const int count = (int)min((int64_t)kVec, n - e0);
-    const bool vec = vec_ok != 0 && count == kVec;
-    float v[kVec];
-    load_state8<SRS_FMT_F32>(x, e0, count, vec, v);
-    store_state8<OF>(y, e0, count, vec, v, base + (uint32_t)e0, stochastic != 0);
+  if (!stochastic) {
+    const int64_t stride = (int64_t)gridDim.x * kThreads * kVec;
+    for (int64_t e0 = ((int64_t)blockIdx.x * kThreads + threadIdx.x) * kVec; e0 < n;
+         e0 += stride) {
+      const int count = (int)min((int64_t)kVec, n - e0);
+      const bool vec = vec_ok != 0 && count == kVec;
+      float v[kVec];
+      load_state8<SRS_FMT_F32>(x, e0, count, vec, v);
+      store_state8<OF>(y, e0, count, vec, v, 0u, false);
+    }
+    return;
+  }
+  extern __shared__ __align__(16) char stage_mem[];
+  const int64_t n_tiles = (n + kTile - 1) / kTile;
+  int64_t tile = n_tiles * blockIdx.x / gridDim.x;
+  const int64_t last = n_tiles * (blockIdx.x + 1) / gridDim.x;
+  int64_t e0 = tile * kTile + (int64_t)threadIdx.x * kVec;
+  if (vec_ok) {
+    const int64_t full_end = min(last, n / kTile);
+    const int n_full = tile < full_end ? (int)(full_end - tile) : 0;
+    const uint32_t slot = (uint32_t)__cvta_generic_to_shared(stage_mem) + threadIdx.x * kVec * 4;
+    if (n_full > 0) cp_async_chunk<kVec * 4>(slot, x + e0);
+    cp_async_commit();
+    for (int i = 0; i < n_full; ++i, e0 += kTile) {
+      if (i + 1 < n_full)
+        cp_async_chunk<kVec * 4>(slot + ((i + 1) & 1) * kCastStageBytes, x + e0 + kTile);
+      cp_async_commit();
+      cp_async_wait_stage();
+      const uint4* s = reinterpret_cast<const uint4*>(stage_mem + (i & 1) * kCastStageBytes +
+                                                      threadIdx.x * kVec * 4);
+      const uint4 a = s[0], b = s[1];
+      const float v[kVec] = {__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z),
+                             __uint_as_float(a.w), __uint_as_float(b.x), __uint_as_float(b.y),
+                             __uint_as_float(b.z), __uint_as_float(b.w)};
+      store_state8<OF>(y, e0, kVec, true, v, base + (uint32_t)e0, true);
+    }
+    tile += n_full;
+  }
+  for (; tile < last; ++tile, e0 += kTile) {
+    if (e0 < n) {
+      const int count = (int)min((int64_t)kVec, n - e0);
+      const bool vec = vec_ok != 0 && count == kVec;
+      float v[kVec];
+      load_state8<SRS_FMT_F32>(x, e0, count, vec, v);
+      store_state8<OF>(y, e0, count, vec, v, base + (uint32_t)e0, true);
+    }
   }
 }
 
