@@ -25,6 +25,9 @@ Other workloads of the same path (one GPU; not the headline):
                            124,439,808 FP32 params, BF16 stochastic momentum)
     --workload cast        the standalone cast, FP32 -> BF16/FP16/E4M3/E5M2 x
                            {stochastic, nearest}, one line per target and rule
+    --workload adamw-70b   AdamW at the Llama-3-70B shape with FP16 stochastic
+                           states on 4 or 8 GPUs, everything sharded (see
+                           run_adamw_70b)
 """
 
 from __future__ import annotations
@@ -70,10 +73,12 @@ def parse_args(argv=None):
     parser.add_argument("--no-embeddings", action="store_true",
                         help="drop the two 128256x4096 matrices (profiling case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast"),
+    parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast", "adamw-70b"),
                         default="adamw-8b")
-    parser.add_argument("--gather", choices=("fused", "nccl"), default="fused",
+    parser.add_argument("--gather", choices=("auto", "fused", "copy", "nccl"), default="auto",
                         help="how the sharded step reassembles the parameters at N>1")
+    parser.add_argument("--chunks", type=int, default=32,
+                        help="tile chunks of the pipelined exchange (--gather copy)")
     parser.add_argument("--cast-elems", type=int, default=1 << 30,
                         help="elements of the cast workload (FP32 input)")
     return parser.parse_args(argv)
@@ -179,7 +184,7 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload --
 
-def build_workload(world, rank, layers=32, embeddings=True, gather="fused"):
+def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunks=32):
     """Flat BF16 parameter and gradient buffers holding the 291 tensors; the
     optimizer (ZeRO-1 when world > 1) over views of them."""
     import torch
@@ -208,7 +213,7 @@ def build_workload(world, rank, layers=32, embeddings=True, gather="fused"):
     fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn, "stochastic"),
            "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
     opt = ZeroAdamW(params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1,
-                    state_format=fmt, seed=7, gather=gather)
+                    state_format=fmt, seed=7, gather=gather, chunks=chunks)
     return opt, params, flat_p, flat_g, total
 
 
@@ -305,7 +310,8 @@ def run_b200(args):
     world, rank = init_distributed(args.gpus)
     peak, peak_source = measured_hbm_peak()
     opt, params, flat_p, flat_g, total = build_workload(world, rank, args.layers,
-                                                        not args.no_embeddings, args.gather)
+                                                        not args.no_embeddings, args.gather,
+                                                        args.chunks)
     local = opt.local_numel()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -333,6 +339,8 @@ def run_b200(args):
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",
                    "gather": {"fused": "updated parameters stored into every peer replica by "
                                        "the step kernel (NVLink peer stores)",
+                              "copy": "copy engines send each chunk of updated parameters to "
+                                      "the peers while the next chunk is updated",
                               "nccl": "NCCL all-gather after the step",
                               "none": "one rank"}[opt.gather_mode],
                    "global_batch": None, "seq_len": None,
@@ -469,6 +477,132 @@ def run_cast(args):
             del out
 
 
+def run_adamw_70b(args):
+    """AdamW at the Llama-3-70B shape: 723 tensors,
+    70,553,706,496 BF16 parameters in two groups (vectors: weight decay 0,
+    AdamW step 5; matrices: weight decay 0.1, AdamW step 6), BF16 gradients,
+    FP16 stochastic moments, seed 3.
+
+    A replicated BF16 copy of the parameters (141 GB) plus full gradients do not
+    fit in one B200, so every rank holds only its shard of the flat parameter
+    buffer (in parameter-group order), of the gradients (as after a
+    reduce-scatter) and of the states.  The step is the fused kernel over the
+    rank's rows (one launch per group) followed by the all-gather of the
+    updated parameters, in chunks through one reused 16 GB staging buffer (the
+    way a sharded model streams its parameters); both are timed."""
+    import torch
+    import torch.distributed as dist
+
+    from sr_states.cuda import _native
+    from sr_states.cuda._fused import adamw_hparams, rng_words
+    from sr_states.cuda._tables import DeviceTable, Update, build_table, upload
+    from sr_states.shapes import llama3_70b
+
+    world, rank = init_distributed(args.gpus)
+    if world < 4:
+        raise SystemExit("the 70B workload needs at least 4 GPUs (memory)")
+    peak, peak_source = measured_hbm_peak()
+    shapes = [s for _, s in llama3_70b()]
+    ordered = [s for s in shapes if len(s) == 1] + [s for s in shapes if len(s) > 1]
+    numels = [math.prod(s) for s in ordered]
+    n_vectors = sum(1 for s in ordered if len(s) == 1)
+    total = sum(numels)
+    unit = world * 64
+    shard = -(-total // unit) * unit // world
+    lo, hi = rank * shard, (rank + 1) * shard
+    device = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=device).manual_seed(3 + rank)
+    p = torch.empty(shard, dtype=torch.bfloat16, device=device).normal_(0, 0.02, generator=gen)
+    g = torch.empty(shard, dtype=torch.bfloat16, device=device).normal_(0, 1e-4, generator=gen)
+    m = torch.zeros(shard, dtype=torch.float16, device=device)
+    v = torch.zeros(shard, dtype=torch.float16, device=device)
+    groups = ([], [])  # (vectors, matrices): updates of this rank's pieces
+    offset = 0
+    for index, n in enumerate(numels):
+        a, b = max(lo, offset), min(hi, offset + n)
+        if a < b:
+            s, e = a - lo, b - lo
+            groups[0 if index < n_vectors else 1].append(
+                Update((p[s:e], g[s:e], m[s:e], v[s:e]), index, e - s, a - offset, None))
+        offset += n
+    tables = []
+    for updates in groups:
+        if updates:
+            host = build_table(updates, [0] * len(updates), 2048)
+            n_tiles = int(host["tile_begin"][-1] + -(-host["numel"][-1] // 2048))
+            tables.append(DeviceTable(host, upload(host, device), len(host), n_tiles))
+        else:
+            tables.append(None)
+    launcher = _native.launcher()
+    launcher.check_device(device)
+    chunk = min(shard, (16 * 10**9 // 2) // world)  # elements per rank and chunk
+    staging = torch.empty(world * chunk, dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream()
+    settings = ((0.0, 5), (0.1, 6))  # (weight decay, AdamW step at the first timed step)
+
+    def one_step(i):
+        rng = rng_words(3, 7 + i)
+        for table, (wd, step) in zip(tables, settings):
+            if table is not None:
+                hp = adamw_hparams(3e-4, (0.9, 0.999), 1e-8, wd, (step + i,))
+                launcher.adamw_multi(table, table.n_rows, table.n_tiles, 2, 1, 2, 1, hp, rng,
+                                     stream.cuda_stream)
+        marks[i][1].record(stream)
+        for k in range(0, shard, chunk):
+            c = min(chunk, shard - k)
+            dist.all_gather_into_tensor(staging[:world * c], p[k:k + c])
+
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(3)]
+             for _ in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        marks[i][0].record(stream)
+        one_step(i)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")
+        start.record(stream)
+        for i in range(args.warmup, args.warmup + args.steps):
+            marks[i][0].record(stream)
+            one_step(i)
+            marks[i][2].record(stream)
+        end.record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
+    timed = marks[args.warmup:]
+    update_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b, _ in timed), world)
+    gather_ms = max_over_ranks(statistics.mean(b.elapsed_time(c) for _, b, c in timed), world)
+    bytes_per_param = 14  # read p 2, g 2, m 2, v 2; write p 2, m 2, v 2
+    achieved = bytes_per_param * shard / (update_ms / 1e3) / 1e9
+    line = {
+        "metric": "AdamW-SR step params/sec & HBM GB/s at 70B shape", "value": total / (ms / 1e3),
+        "unit": "params/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama3-70b AdamW-SR optimizer step (BASELINE config 5)",
+                   "params": total, "tensors": len(ordered), "param_dtype": "bf16",
+                   "grad_dtype": "bf16", "exp_avg": "float16 stochastic",
+                   "exp_avg_sq": "float16 stochastic",
+                   "groups": "vectors wd 0 (AdamW step 5), matrices wd 0.1 (AdamW step 6)",
+                   "parallelism": f"sharded parameters, gradients and states over {world} GPUs; "
+                                  "NCCL all-gather of the parameters in chunks through a "
+                                  f"{staging.numel() * 2 / 1e9:.0f} GB staging buffer",
+                   "l2": f"{bytes_per_param * shard / 1e9:.0f} GB moved per step and GPU; no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
+                     "kernel": "srs::adamw_kernel<F16,F16>", "kernel_ms": update_ms,
+                     "bytes_per_param": bytes_per_param, "params_per_launch": shard},
+        "gather_ms": gather_ms, "gpu_launches": sum(t is not None for t in tables) * args.steps,
+        "clocks": clocks.report()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def run_reference(args):
     """The reference arm: the CPU restatement of the reference algorithm (the reference
     itself is Python on PyTorch's CPU kernels and does not travel to this box) on all
@@ -501,6 +635,8 @@ def main(argv=None):
         run_sgdm_gpt2(args)
     elif args.workload == "cast":
         run_cast(args)
+    elif args.workload == "adamw-70b":
+        run_adamw_70b(args)
     else:
         run_b200(args)
 

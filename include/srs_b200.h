@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define SRS_ABI_VERSION 3
+#define SRS_ABI_VERSION 4
 
 /* ---- status codes ------------------------------------------------------ */
 #define SRS_OK 0
@@ -177,6 +177,24 @@ int srs_sgdm_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, 
                           int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
                           uint32_t uniform_kind, const srs_peers* peers, int grid_ctas,
                           void* stream);
+
+/* ---- tile ranges and copies for a pipelined exchange ---------------------
+ * No counterpart in the reference.  The same steps over the tiles
+ * [tile_lo, tile_hi) of the table only (0 <= tile_lo <= tile_hi <= n_tiles):
+ * a sharded step split into chunks, each chunk's updated parameters sent to
+ * the peers by srs_copy_async (a device-to-device cudaMemcpyAsync, done by
+ * the copy engines) while the next chunk is updated.
+ */
+int srs_adamw_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
+                          int64_t tile_hi, int m_format, int m_rule, int v_format, int v_rule,
+                          const srs_adamw_hparams* hp, const srs_rng* rng, uint32_t uniform_kind,
+                          int grid_ctas, void* stream);
+
+int srs_sgdm_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
+                         int64_t tile_hi, int u_format, int u_rule, const srs_sgdm_hparams* hp,
+                         const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream);
+
+int srs_copy_async(void* dst, const void* src, uint64_t bytes, void* stream);
 
 /* Peer mappings (CUDA IPC) of the buffers above.  srs_ipc_export writes a
  * handle of the allocation holding device address `p` (SRS_IPC_HANDLE_BYTES

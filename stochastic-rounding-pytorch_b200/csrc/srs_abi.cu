@@ -269,10 +269,18 @@ static int check_peers(const srs_peers* peers) {
   return SRS_OK;
 }
 
+static int check_range(int64_t n_tiles, int64_t tile_lo, int64_t tile_hi) {
+  if (tile_lo < 0 || tile_lo > tile_hi || tile_hi > n_tiles)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "tile range [%lld, %lld) is not inside [0, %lld)",
+                (long long)tile_lo, (long long)tile_hi, (long long)n_tiles);
+  return SRS_OK;
+}
+
 static int adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,
                        int m_rule, int v_format, int v_rule, const srs_adamw_hparams* hp,
                        const srs_rng* rng, uint32_t uniform_kind, const srs_peers* peers,
-                       int grid_ctas, void* stream, const char* what) {
+                       int grid_ctas, void* stream, const char* what, int64_t tile_lo = 0,
+                       int64_t tile_hi = -1) {
   g_error[0] = '\0';
   if (!valid_format(m_format) || !valid_format(v_format))
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format (%d, %d)", m_format, v_format);
@@ -282,9 +290,13 @@ static int adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int
   if (int rc = check_hp_classes(hp->n_step_classes)) return rc;
   if (peers != nullptr)
     if (int rc = check_peers(peers)) return rc;
-  if (n_tiles == 0) return SRS_OK;
+  if (tile_hi < 0) tile_hi = n_tiles;
+  if (int rc = check_range(n_tiles, tile_lo, tile_hi)) return rc;
+  if (tile_lo == tile_hi) return SRS_OK;
   if (int rc = check_device()) return rc;
   AdamWArgs a{};
+  a.tile_lo = tile_lo;
+  a.tile_hi = tile_hi;
   a.hp = *hp;
   fill_reciprocals(*hp, a);
   a.rng = *rng;
@@ -300,7 +312,7 @@ static int adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int
 static int sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_format,
                       int u_rule, const srs_sgdm_hparams* hp, const srs_rng* rng,
                       uint32_t uniform_kind, const srs_peers* peers, int grid_ctas, void* stream,
-                      const char* what) {
+                      const char* what, int64_t tile_lo = 0, int64_t tile_hi = -1) {
   g_error[0] = '\0';
   if (!valid_format(u_format))
     return fail(SRS_ERR_INVALID_ARGUMENT, "unknown state format %d", u_format);
@@ -308,9 +320,13 @@ static int sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int 
   if (int rc = check_multi(rows, n_rows, n_tiles, hp, rng)) return rc;
   if (peers != nullptr)
     if (int rc = check_peers(peers)) return rc;
-  if (n_tiles == 0) return SRS_OK;
+  if (tile_hi < 0) tile_hi = n_tiles;
+  if (int rc = check_range(n_tiles, tile_lo, tile_hi)) return rc;
+  if (tile_lo == tile_hi) return SRS_OK;
   if (int rc = check_device()) return rc;
   SgdmArgs a{};
+  a.tile_lo = tile_lo;
+  a.tile_hi = tile_hi;
   a.hp = *hp;
   a.rng = *rng;
   a.u_stochastic = u_rule;
@@ -350,6 +366,31 @@ int srs_sgdm_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, 
   if (peers == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null peers");
   return sgdm_multi(rows, n_rows, n_tiles, u_format, u_rule, hp, rng, uniform_kind, peers,
                     grid_ctas, stream, "srs_sgdm_multi_gather launch");
+}
+
+int srs_adamw_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
+                          int64_t tile_hi, int m_format, int m_rule, int v_format, int v_rule,
+                          const srs_adamw_hparams* hp, const srs_rng* rng, uint32_t uniform_kind,
+                          int grid_ctas, void* stream) {
+  return adamw_multi(rows, n_rows, n_tiles, m_format, m_rule, v_format, v_rule, hp, rng,
+                     uniform_kind, nullptr, grid_ctas, stream, "srs_adamw_multi_range launch",
+                     tile_lo, tile_hi);
+}
+
+int srs_sgdm_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
+                         int64_t tile_hi, int u_format, int u_rule, const srs_sgdm_hparams* hp,
+                         const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream) {
+  return sgdm_multi(rows, n_rows, n_tiles, u_format, u_rule, hp, rng, uniform_kind, nullptr,
+                    grid_ctas, stream, "srs_sgdm_multi_range launch", tile_lo, tile_hi);
+}
+
+int srs_copy_async(void* dst, const void* src, uint64_t bytes, void* stream) {
+  g_error[0] = '\0';
+  if (bytes == 0) return SRS_OK;
+  if (dst == nullptr || src == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null pointer");
+  const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice,
+                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_copy_async");
 }
 
 // Base of the allocation holding a device address, through the driver's
@@ -438,6 +479,8 @@ int srs_adamw_single(const srs_row* row, int m_format, int m_rule, int v_format,
   a.inline_row = *row;
   a.inline_row.tile_begin = 0;
   a.inline_row.flags &= ~(0xFFu << SRS_ROW_CLASS_SHIFT);
+  a.tile_lo = 0;
+  a.tile_hi = n_tiles;
   a.hp = *hp;
   fill_reciprocals(*hp, a);
   a.rng.key_mode = SRS_KEY_GIVEN;
@@ -464,6 +507,8 @@ int srs_sgdm_single(const srs_row* row, int u_format, int u_rule, const srs_sgdm
   SgdmArgs a{};
   a.inline_row = *row;
   a.inline_row.tile_begin = 0;
+  a.tile_lo = 0;
+  a.tile_hi = n_tiles;
   a.hp = *hp;
   a.rng.key_mode = SRS_KEY_GIVEN;
   a.u_stochastic = u_rule;
@@ -604,6 +649,8 @@ extern "C" int srs_adamw_multi_noalloc(const srs_row* host_rows, int64_t n_rows,
   a.rng = *rng;
   a.m_stochastic = m_rule;
   a.v_stochastic = v_rule;
+  a.tile_lo = 0;
+  a.tile_hi = n_tiles;
   e = kAdamW[m_format][v_format](table, n_rows, n_tiles, kind_index(kind), a, grid_ctas, s);
   return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_adamw_multi_noalloc launch");
 }

@@ -14,7 +14,7 @@ static cudaError_t launch_kind(const srs_row* rows, int64_t n_rows, int64_t n_ti
   cudaError_t err = cudaSuccess;
   constexpr int smem = adamw_stage_bytes<MF, VF, KIND>();
   const void* kernel = reinterpret_cast<const void*>(&adamw_kernel<MF, VF, KIND>);
-  const int grid = grid_for(kernel, n_tiles, grid_ctas, &err, smem);
+  const int grid = grid_for(kernel, a.tile_hi - a.tile_lo, grid_ctas, &err, smem);
   if (err != cudaSuccess) return err;
   adamw_kernel<MF, VF, KIND><<<grid, kThreads, smem, stream>>>(rows, n_rows, n_tiles, a);
   return cudaGetLastError();

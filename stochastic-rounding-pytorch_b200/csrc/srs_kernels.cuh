@@ -38,6 +38,7 @@ struct AdamWArgs {
   int32_t m_stochastic;
   int32_t v_stochastic;
   srs_peers peers;  // replicas that receive the updated parameters (n_peers == 0: none)
+  int64_t tile_lo, tile_hi;  // the launch covers tiles [tile_lo, tile_hi) of the table
 };
 
 struct SgdmArgs {
@@ -46,6 +47,7 @@ struct SgdmArgs {
   srs_rng rng;
   int32_t u_stochastic;
   srs_peers peers;
+  int64_t tile_lo, tile_hi;
 };
 
 // A row as held (uniformly) by one CTA while it walks that row's tiles.
@@ -130,10 +132,11 @@ struct TileRange {
 };
 
 __device__ __forceinline__ TileRange cta_tiles(const srs_row* rows, int64_t n_rows,
-                                               int64_t n_tiles) {
+                                               int64_t tile_lo, int64_t tile_hi) {
   TileRange t;
-  t.tile = n_tiles * blockIdx.x / gridDim.x;
-  t.last = n_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int64_t span = tile_hi - tile_lo;
+  t.tile = tile_lo + span * blockIdx.x / gridDim.x;
+  t.last = tile_lo + span * (blockIdx.x + 1) / gridDim.x;
   t.r = (rows != nullptr && t.tile < t.last) ? find_row(rows, n_rows, t.tile) : 0;
   return t;
 }
@@ -489,7 +492,7 @@ template <int MF, int VF, int KIND>
 __global__ void __launch_bounds__(kThreads, SRS_ADAMW_MIN_CTAS)
     adamw_kernel(const srs_row* __restrict__ rows, int64_t n_rows, int64_t n_tiles,
                  const __grid_constant__ AdamWArgs a) {
-  TileRange t = cta_tiles(rows, n_rows, n_tiles);
+  TileRange t = cta_tiles(rows, n_rows, a.tile_lo, a.tile_hi);
   if (t.tile >= t.last) return;
   do {
     const RowView rv = make_view(rows != nullptr ? load_row(rows + t.r) : a.inline_row, a);
@@ -610,7 +613,7 @@ template <int UF, int KIND>
 __global__ void __launch_bounds__(kThreads)
     sgdm_kernel(const srs_row* __restrict__ rows, int64_t n_rows, int64_t n_tiles,
                 const __grid_constant__ SgdmArgs a) {
-  TileRange t = cta_tiles(rows, n_rows, n_tiles);
+  TileRange t = cta_tiles(rows, n_rows, a.tile_lo, a.tile_hi);
   if (t.tile >= t.last) return;
   do {
     const RowView rv = make_view(rows != nullptr ? load_row(rows + t.r) : a.inline_row, a);

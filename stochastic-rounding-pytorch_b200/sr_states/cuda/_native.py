@@ -108,12 +108,22 @@ _SIGNATURES = {
                                ctypes.POINTER(SrsSgdmHparams), ctypes.POINTER(SrsRng),
                                ctypes.c_uint32, ctypes.POINTER(SrsPeers), ctypes.c_int, _P],
                               ctypes.c_int),
+    "srs_adamw_multi_range": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                               ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_int, ctypes.POINTER(SrsAdamWHparams),
+                               ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.c_int, _P],
+                              ctypes.c_int),
+    "srs_sgdm_multi_range": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                              ctypes.c_int, ctypes.c_int, ctypes.POINTER(SrsSgdmHparams),
+                              ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.c_int, _P],
+                             ctypes.c_int),
+    "srs_copy_async": ([_P, _P, ctypes.c_uint64, _P], ctypes.c_int),
     "srs_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "srs_ipc_import": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "srs_ipc_close": ([_P], ctypes.c_int),
 }
 NOALLOC_MAX_ROWS = 4096
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lock = threading.Lock()
 _library = None
@@ -180,9 +190,14 @@ class NativeLauncher:
                                        stream))
 
     def adamw_multi(self, table, n_rows, n_tiles, m_fmt, m_rule, v_fmt, v_rule, hp, rng, stream,
-                    grid_ctas=0, peers=None):
+                    grid_ctas=0, peers=None, tiles=None):
         lib = load_library()
-        if peers is None:
+        if tiles is not None:
+            _check(lib.srs_adamw_multi_range(table.device_ptr, n_rows, n_tiles, tiles[0],
+                                             tiles[1], m_fmt, m_rule, v_fmt, v_rule,
+                                             ctypes.byref(hp), ctypes.byref(rng),
+                                             table.uniform_kind, grid_ctas, stream))
+        elif peers is None:
             _check(lib.srs_adamw_multi(table.device_ptr, n_rows, n_tiles, m_fmt, m_rule, v_fmt,
                                        v_rule, ctypes.byref(hp), ctypes.byref(rng),
                                        table.uniform_kind, grid_ctas, stream))
@@ -193,9 +208,13 @@ class NativeLauncher:
                                               stream))
 
     def sgdm_multi(self, table, n_rows, n_tiles, u_fmt, u_rule, hp, rng, stream, grid_ctas=0,
-                   peers=None):
+                   peers=None, tiles=None):
         lib = load_library()
-        if peers is None:
+        if tiles is not None:
+            _check(lib.srs_sgdm_multi_range(table.device_ptr, n_rows, n_tiles, tiles[0], tiles[1],
+                                            u_fmt, u_rule, ctypes.byref(hp), ctypes.byref(rng),
+                                            table.uniform_kind, grid_ctas, stream))
+        elif peers is None:
             _check(lib.srs_sgdm_multi(table.device_ptr, n_rows, n_tiles, u_fmt, u_rule,
                                       ctypes.byref(hp), ctypes.byref(rng), table.uniform_kind,
                                       grid_ctas, stream))
@@ -204,6 +223,10 @@ class NativeLauncher:
                                              ctypes.byref(hp), ctypes.byref(rng),
                                              table.uniform_kind, ctypes.byref(peers), grid_ctas,
                                              stream))
+
+    def copy_async(self, dst, src, nbytes, stream):
+        """Device-to-device copy on ``stream`` (peer memory included)."""
+        _check(load_library().srs_copy_async(dst, src, nbytes, stream))
 
     def ipc_export(self, ptr):
         """(handle bytes, offset of ptr in its allocation) for mapping in a peer process."""

@@ -92,6 +92,42 @@ def test_peer_stores_fill_replicas_and_leave_results_unchanged(cuda_device, kind
         assert torch.all(rep[rows:] == 7.0)
 
 
+@pytest.mark.parametrize("kind", ["adamw", "sgdm"])
+def test_tile_range_launches_equal_one_launch(cuda_device, kind):
+    """A table launched as consecutive tile ranges (the chunks of a pipelined
+    exchange) gives the bits of one launch over the whole table."""
+    launcher = _native.launcher()
+    states = ((torch.float8_e4m3fn, torch.bfloat16) if kind == "adamw" else (torch.bfloat16,))
+    flat, updates = _workload(cuda_device, torch.bfloat16, states)
+    flat_ref, updates_ref = _clone(updates, flat)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    rng = rng_words(5, 9)
+    for ups, ranged in ((updates, True), (updates_ref, False)):
+        table = _table(ups, cuda_device)
+        cuts = [0, 1, 7, 40, table.n_tiles] if ranged else [0, table.n_tiles]
+        for lo, hi in zip(cuts, cuts[1:]):
+            extra = {"tiles": (lo, hi)} if ranged else {}
+            if kind == "adamw":
+                hp = adamw_hparams(1e-3, (0.9, 0.999), 1e-8, 0.01, (1,))
+                launcher.adamw_multi(table, table.n_rows, table.n_tiles, 3, 1, 1, 1, hp, rng,
+                                     stream, **extra)
+            else:
+                launcher.sgdm_multi(table, table.n_rows, table.n_tiles, 1, 1,
+                                    sgdm_hparams(1e-2, 0.9), rng, stream, **extra)
+    torch.cuda.synchronize(cuda_device)
+    assert np.array_equal(_bits(flat), _bits(flat_ref))
+    for u, r in zip(updates, updates_ref):
+        for a, b in zip(u.tensors[2:], r.tensors[2:]):
+            assert np.array_equal(_bits(a), _bits(b))
+    dst = torch.zeros_like(flat)
+    launcher.copy_async(dst.data_ptr(), flat.data_ptr(), 1000 * 2, stream)
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(dst[:1000], flat[:1000]) and torch.all(dst[1000:] == 0)
+    with pytest.raises(ValueError, match="tile range"):
+        launcher.sgdm_multi(table, table.n_rows, table.n_tiles, 1, 1, sgdm_hparams(1e-2, 0.9),
+                            rng, stream, tiles=(3, table.n_tiles + 1))
+
+
 def test_peer_count_is_checked(cuda_device):
     launcher = _native.launcher()
     flat, updates = _workload(cuda_device, torch.bfloat16, (torch.bfloat16,))
@@ -121,7 +157,7 @@ def _two_rank_worker(rank, world, port, results):
         fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn, "stochastic"),
                "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
         runs = {}
-        for mode in ("fused", "nccl", "single"):
+        for mode in ("fused", "copy", "nccl", "single"):
             gen = torch.Generator().manual_seed(5)
             params = []
             for n in SIZES:
@@ -141,21 +177,21 @@ def _two_rank_worker(rank, world, port, results):
             runs[mode] = [p.detach().view(torch.uint16).cpu().numpy().copy() for p in params]
             if mode != "single":
                 opt.close()
-        results[rank] = (runs["fused_mode"], runs["nccl_mode"],
-                         all(np.array_equal(a, b) for a, b in zip(runs["fused"], runs["single"])),
-                         all(np.array_equal(a, b) for a, b in zip(runs["nccl"], runs["single"])))
+        same = {m: all(np.array_equal(a, b) for a, b in zip(runs[m], runs["single"]))
+                for m in ("fused", "copy", "nccl")}
+        results[rank] = ((runs["fused_mode"], runs["copy_mode"], runs["nccl_mode"]), same)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_fused_gather_equals_nccl_and_unsharded_steps():
+def test_two_ranks_fused_and_copy_gathers_equal_nccl_and_unsharded_steps():
     import torch.multiprocessing as mp
 
     manager = mp.Manager()
     results = manager.dict()
     mp.spawn(_two_rank_worker, args=(2, 29533, results), nprocs=2, join=True)
     for rank in range(2):
-        fused_mode, nccl_mode, fused_ok, nccl_ok = results[rank]
-        assert (fused_mode, nccl_mode) == ("fused", "nccl")
-        assert fused_ok and nccl_ok
+        modes, same = results[rank]
+        assert modes == ("fused", "copy", "nccl")
+        assert same == {"fused": True, "copy": True, "nccl": True}
