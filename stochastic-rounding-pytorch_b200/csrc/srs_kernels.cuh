@@ -336,6 +336,8 @@ __device__ __forceinline__ void adamw_update_fast(float (&p)[kVec], const float 
     const float2 nq0 = mul2_rn(n2, ny1);
     const float2 res = fma2_rn(den, nq0, n2);
     const float2 nq = fma2_rn(res, ny1, nq0);  // -(num / den)
+    // Scalar, like mul_add_rn2: a packed p*decay feeding a packed add or sub is
+    // contracted into one FMA by ptxas (even written as fma(p, decay, -0)).
     p[2 * i] = __fadd_rn(__fmul_rn(p[2 * i], decay.x), -nq.x);
     p[2 * i + 1] = __fadd_rn(__fmul_rn(p[2 * i + 1], decay.y), -nq.y);
   }
