@@ -25,7 +25,12 @@ the copy engines send each finished range to the peers while the next one is
 updated.  The default, ``"auto"``, takes ``"copy"`` with one peer and
 ``"fused"`` with more (the faster of the two on B200 in each case).
 
-Gradients must be complete on every rank (already all-reduced), as in ZeRO-1.
+Gradients must be complete on every rank (already all-reduced), as in ZeRO-1,
+unless the optimizer is built with ``grads="reduce_scatter"``: then every
+``p.grad`` is a view into a flat gradient buffer laid out like the parameters,
+backward accumulates into it, and ``reduce_scatter_grads()`` reduces each
+rank's shard in place (one reduce-scatter per buffer) so that the step reads
+only its own reduced gradients; ``zero_grad()`` zeroes the buffers in place.
 
 Checkpoints: ``state_dict()`` gathers the shards into the unsharded layout of
 AdamWReferenceSR / SGDMReferenceSR (every state in its parameter's shape), so
@@ -194,9 +199,12 @@ class _ChunkedExchange:
 class _ZeroMixin:
     """ZeRO-1 behaviour for a fused StateOptimizer subclass (see module docstring)."""
 
-    def __init__(self, params, *args, process_group=None, gather="auto", chunks=32, **kwargs):
+    def __init__(self, params, *args, process_group=None, gather="auto", chunks=32,
+                 grads="full", **kwargs):
         if gather not in ("auto", "fused", "copy", "nccl"):
             raise ValueError(f"gather must be 'auto', 'fused', 'copy' or 'nccl', got {gather!r}")
+        if grads not in ("full", "reduce_scatter"):
+            raise ValueError(f"grads must be 'full' or 'reduce_scatter', got {grads!r}")
         super().__init__(params, *args, **kwargs)
         self._group = process_group
         initialized = torch.distributed.is_available() and torch.distributed.is_initialized()
@@ -206,6 +214,12 @@ class _ZeroMixin:
         self._layout = FlatLayout(ordered, self._world, self._rank)
         self._events: list = []
         self._timed: list = []
+        self._grad_buffers: dict[torch.dtype, torch.Tensor] = {}
+        if grads == "reduce_scatter":
+            for dtype, buffer in self._layout.buffers.items():
+                self._grad_buffers[dtype] = torch.zeros_like(buffer)
+            for p in ordered:
+                p.grad = self._grad_slot(p)
         self._peer_bases: list[int] = []
         self._srs_peers = None
         self._srs_exchange = None
@@ -293,6 +307,55 @@ class _ZeroMixin:
 
     def _barrier(self):
         torch.distributed.all_reduce(self._sync, group=self._group)
+
+    # ------------------------------------------------------------ gradients --
+
+    def _grad_slot(self, p):
+        dtype, offset = self._layout.place[id(p)]
+        return self._grad_buffers[dtype][offset:offset + p.numel()].view(p.shape)
+
+    @torch.no_grad()
+    def zero_grad(self, set_to_none: bool = True):
+        """With ``grads="reduce_scatter"`` the flat gradient buffers are zeroed in
+        place (the gradients stay views into them); otherwise as in PyTorch."""
+        if not self._grad_buffers:
+            return super().zero_grad(set_to_none)
+        for buffer in self._grad_buffers.values():
+            buffer.zero_()
+        for g in self.param_groups:
+            for p in g["params"]:
+                p.grad = self._grad_slot(p)
+
+    @torch.no_grad()
+    def reduce_scatter_grads(self, op: str = "mean"):
+        """Reduce every rank's gradients (``"mean"`` or ``"sum"``) into this rank's
+        shard of the flat gradient buffers, in place.  A collective; requires
+        ``grads="reduce_scatter"``.  Gradients that backward placed outside the
+        buffers (after ``zero_grad(set_to_none=True)`` elsewhere) are copied in."""
+        if not self._grad_buffers:
+            raise RuntimeError("reduce_scatter_grads requires grads='reduce_scatter'")
+        if op not in ("mean", "sum"):
+            raise ValueError(f"op must be 'mean' or 'sum', got {op!r}")
+        for g in self.param_groups:
+            for p in g["params"]:
+                slot = self._grad_slot(p)
+                if p.grad is None:
+                    slot.zero_()
+                elif p.grad.data_ptr() != slot.data_ptr() or p.grad.shape != slot.shape:
+                    slot.copy_(p.grad)
+                p.grad = slot
+        if self._world == 1:
+            return
+        dist = torch.distributed
+        gloo = dist.get_backend(self._group) == "gloo"
+        for dtype, buffer in self._grad_buffers.items():
+            lo, hi = self._layout.shard(dtype)
+            if gloo:  # gloo has no reduce-scatter of a flat tensor: reduce everything
+                dist.all_reduce(buffer, group=self._group)
+            else:
+                dist.reduce_scatter_tensor(buffer[lo:hi], buffer, group=self._group)
+            if op == "mean":
+                buffer[lo:hi].div_(self._world)
 
     # ---------------------------------------------------------- checkpoints --
 

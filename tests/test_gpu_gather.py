@@ -179,6 +179,36 @@ def _two_rank_worker(rank, world, port, results):
                 opt.close()
         same = {m: all(np.array_equal(a, b) for a, b in zip(runs[m], runs["single"]))
                 for m in ("fused", "copy", "nccl")}
+        # Gradients reduce-scattered by NCCL (small integers times 2^-10 summed exactly)
+        # equal the unsharded step on the mean gradients.
+        outs = {}
+        for mode in ("rs", "single"):
+            gen = torch.Generator().manual_seed(6)
+            params = [torch.nn.Parameter(torch.randn(n, generator=gen).to("cuda", torch.bfloat16))
+                      for n in SIZES]
+            if mode == "rs":
+                opt = ZeroAdamW(params, lr=1e-3, state_format=fmt, seed=9, grads="reduce_scatter")
+                opt.zero_grad()
+                for i, p in enumerate(params):
+                    g = torch.Generator().manual_seed(100 * rank + i)
+                    p.grad.copy_((torch.randint(-8, 9, (p.numel(),), generator=g) / 1024.0)
+                                 .to("cuda", torch.bfloat16))
+                opt.reduce_scatter_grads("mean")
+            else:
+                from sr_states import AdamWReferenceSR
+
+                opt = AdamWReferenceSR(params, lr=1e-3, state_format=fmt, seed=9)
+                for i, p in enumerate(params):
+                    total = sum(torch.randint(-8, 9, (p.numel(),),
+                                              generator=torch.Generator().manual_seed(100 * r + i))
+                                / 1024.0 for r in range(world))
+                    p.grad = (total / world).to("cuda", torch.bfloat16)
+            opt.step()
+            torch.cuda.synchronize()
+            outs[mode] = [p.detach().view(torch.uint16).cpu().numpy().copy() for p in params]
+            if mode == "rs":
+                opt.close()
+        same["reduce_scatter"] = all(np.array_equal(a, b) for a, b in zip(outs["rs"], outs["single"]))
         results[rank] = ((runs["fused_mode"], runs["copy_mode"], runs["nccl_mode"]), same)
     finally:
         dist.destroy_process_group()
@@ -188,10 +218,10 @@ def _two_rank_worker(rank, world, port, results):
 def test_two_ranks_fused_and_copy_gathers_equal_nccl_and_unsharded_steps():
     import torch.multiprocessing as mp
 
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()  # no fork after CUDA is initialised
     results = manager.dict()
     mp.spawn(_two_rank_worker, args=(2, 29533, results), nprocs=2, join=True)
     for rank in range(2):
         modes, same = results[rank]
         assert modes == ("fused", "copy", "nccl")
-        assert same == {"fused": True, "copy": True, "nccl": True}
+        assert same == {"fused": True, "copy": True, "nccl": True, "reduce_scatter": True}

@@ -181,3 +181,70 @@ def test_zero1_checkpoints_gather_to_the_unsharded_layout_and_resume(world):
         if p.is_alive():
             p.kill()
     assert results == {r: "ok" for r in range(world)}, results
+
+
+def _reduce_scatter_worker(rank, world, port, queue):
+    sys.path[:0] = [str(ROOT), str(ROOT / "stochastic-rounding-pytorch_b200"), str(ROOT / "tests")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    from _support import FakeLauncher
+    from sr_states import AdamWReferenceSR
+    from sr_states.cuda import _native
+    from sr_states.distributed import ZeroAdamW
+
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        _native.set_launcher(FakeLauncher())
+        params, _, fmt = _problem()
+        reference = [torch.nn.Parameter(p.detach().clone()) for p in params]
+        ref_opt = AdamWReferenceSR(reference, lr=1e-2, state_format=fmt, seed=11)
+        opt = ZeroAdamW(params, lr=1e-2, state_format=fmt, seed=11, grads="reduce_scatter")
+
+        def rank_grad(p, r, step):
+            # small integers times 2^-10: sums over ranks are exact in any order
+            gen = torch.Generator().manual_seed(1000 * step + 10 * r + p.numel())
+            return (torch.randint(-8, 9, p.shape, generator=gen).float() / 1024).to(p.dtype)
+
+        for step in range(2):
+            opt.zero_grad()
+            for i, p in enumerate(params):
+                if i == 1:
+                    p.grad = rank_grad(p, rank, step)  # a fresh tensor: copied into the buffer
+                else:
+                    p.grad.copy_(rank_grad(p, rank, step))
+            opt.reduce_scatter_grads("mean")
+            opt.step()
+            for q, p in zip(reference, params):
+                total = sum(rank_grad(p, r, step).float() for r in range(world)).to(p.dtype)
+                q.grad = total.div_(world)
+            ref_opt.step()
+        for p, q in zip(params, reference):
+            assert torch.equal(p.detach().view(torch.uint8), q.detach().view(torch.uint8))
+        queue.put((rank, "ok"))
+    except BaseException:  # report, never hang the parent
+        import traceback
+        queue.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_zero_reduce_scattered_gradients_equal_unsharded_mean_gradients(world):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_reduce_scatter_worker, args=(r, world, port, queue))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results == {r: "ok" for r in range(world)}, results
