@@ -274,8 +274,7 @@ __device__ __forceinline__ float rsqrt_approx(float x) {
 //    which also gives the quotient of a zero numerator its sign.
 // Vectors outside the screen take the exact per-element operations instead.
 __device__ __forceinline__ bool adamw_screen(const float (&m1)[kVec], const float (&v1)[kVec],
-                                             float m_floor) {
-  float y[kVec];
+                                             float m_floor, float (&y)[kVec]) {
 #pragma unroll
   for (int j = 0; j < kVec; ++j) y[j] = rsqrt_approx(v1[j]);
   float2 acc = mul2_rn(make_float2(m1[0], m1[1]), make_float2(m1[0], m1[1]));
@@ -318,13 +317,13 @@ __device__ __forceinline__ float2 div_by_uniform(float2 s, const ClassScalars& k
 
 // Parameter update of a screened vector (see adamw_screen); p is overwritten.
 __device__ __forceinline__ void adamw_update_fast(float (&p)[kVec], const float (&m1)[kVec],
-                                                  const float (&v1)[kVec],
+                                                  const float (&v1)[kVec], const float (&y)[kVec],
                                                   const ClassScalars& k, const AdamWArgs& a) {
   const float2 eps = splat(a.hp.eps), decay = splat(a.hp.decay), nss = splat(k.nss);
 #pragma unroll
   for (int i = 0; i < kVec / 2; ++i) {
     const float2 v2 = make_float2(v1[2 * i], v1[2 * i + 1]);
-    const float2 y2 = make_float2(rsqrt_approx(v2.x), rsqrt_approx(v2.y));
+    const float2 y2 = make_float2(y[2 * i], y[2 * i + 1]);
     const float2 g = mul2_rn(v2, y2), h = mul2_rn(y2, splat(0.5f));
     const float2 r = make_float2(__fmaf_rn(-g.x, g.x, v2.x), __fmaf_rn(-g.y, g.y, v2.y));
     const float2 root = fma2_rn(r, h, g);
@@ -417,8 +416,9 @@ __device__ __forceinline__ void adamw8_compute(const RowView& rv, int64_t e0, in
       v[2 * i] = v1.x;
       v[2 * i + 1] = v1.y;
     }
-    if (adamw_screen(m, v, k.m_floor)) {
-      adamw_update_fast(p, m, v, k, a);
+    float y[kVec];
+    if (adamw_screen(m, v, k.m_floor, y)) {
+      adamw_update_fast(p, m, v, y, k, a);
       const uint32_t ctr_m = (uint32_t)e0 + rv.ctr0, ctr_v = (uint32_t)e0 + rv.ctr1;
       store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
       store_state8_screened<MF>(rv.s0, e0, count, VEC, m, ctr_m, a.m_stochastic != 0);
@@ -487,7 +487,11 @@ __device__ __noinline__ void adamw8_generic(const RowView& rv, int64_t e0, int c
 }
 
 #ifndef SRS_ADAMW_MIN_CTAS
-#define SRS_ADAMW_MIN_CTAS 4  // resident CTAs per SM the register budget is sized for
+// Resident CTAs per SM the register budget is sized for: 3 gives 80 registers
+// and no spills; the cp.async double buffer, not the warp count, hides the
+// memory latency (measured: as fast as 4 CTAs with spills, slightly faster
+// once rsqrt(v') is kept from the screen for the update).
+#define SRS_ADAMW_MIN_CTAS 3
 #endif
 
 template <int MF, int VF, int KIND>

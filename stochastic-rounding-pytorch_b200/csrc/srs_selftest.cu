@@ -133,14 +133,15 @@ __global__ void adamw_fast_kernel(uint64_t n_vectors, uint32_t seed, srs::ClassS
       m1[j] = random_scaled(h1, extreme ? -110 : -30, extreme ? 180 : 32, true);
       v1[j] = random_scaled(h2, extreme ? -100 : -50, extreme ? 150 : 55, false);
     }
-    if (!srs::adamw_screen(m1, v1, k.m_floor)) {
+    float y[srs::kVec];
+    if (!srs::adamw_screen(m1, v1, k.m_floor, y)) {
       ++local[2];
       continue;
     }
     float fast[srs::kVec];
 #pragma unroll
     for (int j = 0; j < srs::kVec; ++j) fast[j] = p[j];
-    srs::adamw_update_fast(fast, m1, v1, k, a);
+    srs::adamw_update_fast(fast, m1, v1, y, k, a);
     bool differ = false;
 #pragma unroll
     for (int j = 0; j < srs::kVec; ++j) {
