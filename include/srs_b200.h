@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define SRS_ABI_VERSION 4
+#define SRS_ABI_VERSION 5
 
 /* ---- status codes ------------------------------------------------------ */
 #define SRS_OK 0
@@ -46,6 +46,14 @@ extern "C" {
 /* ---- rounding rules ---------------------------------------------------- */
 #define SRS_RULE_NEAREST 0    /* round to nearest, ties to even */
 #define SRS_RULE_STOCHASTIC 1 /* counter-hash stochastic rounding */
+/* Round toward zero: the format's value of largest magnitude not above |x|,
+ * sign kept (BF16: the high half of the FP32 encoding).  Finite values never
+ * become infinite; +-Inf stays infinite in BF16/FP16 and saturates in FP8; NaN
+ * is stored as under the other rules.  Not a reference built-in: it is the
+ * native implementation a custom rule registered through
+ * register_rounding(..., native="toward_zero") runs (the reference's custom
+ * rules, sr_states/rounding.py:28-66, run as Triton callbacks). */
+#define SRS_RULE_TOWARD_ZERO 2
 
 /* ---- multi-tensor row table -------------------------------------------- */
 #define SRS_ROW_PARAM_BF16 0x1u  /* parameter is BF16 (else FP32) */

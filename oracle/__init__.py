@@ -25,7 +25,7 @@ import numpy as np
 from .build_oracle import LIBRARY, build
 
 F32, BF16, F16, E4M3, E5M2 = 0, 1, 2, 3, 4
-NEAREST, STOCHASTIC = 0, 1
+NEAREST, STOCHASTIC, TOWARD_ZERO = 0, 1, 2
 BITS_DTYPE = {F32: np.uint32, BF16: np.uint16, F16: np.uint16, E4M3: np.uint8, E5M2: np.uint8}
 _MASK32 = 0xFFFFFFFF
 

@@ -187,15 +187,43 @@ static uint32_t bf16_stochastic(float x, uint32_t counter) {
   return rounded >> 16;
 }
 
+/* Round toward zero: the format's value of largest magnitude not above |x|,
+ * sign kept.  Not a reference built-in; it is what a custom rule runs when it
+ * is registered with native="toward_zero".  The reference's own tests register
+ * a rule of that name for BF16 (tests/test_rounding_registry.py:15-17: clear
+ * the low 16 bits of the FP32 encoding, then convert), which this rule equals
+ * on every input except NaNs whose payload lies only in those 16 bits (the
+ * test's rule turns them into +-Inf; here every NaN is stored as the other
+ * BF16 rules store it).  FP16 keeps IEEE round-toward-zero overflow (finite
+ * values end at 65504, +-Inf stays infinite); FP8 saturates like the other
+ * FP8 rules (sr_states/_minifloat.py:45-70). */
+static uint32_t bf16_toward_zero(float x) {
+  if (isnan(x)) return 0xFFFFu;
+  return f2u(x) >> 16;
+}
+
+static uint32_t toward_zero_minifloat(float x, const minifmt* f) {
+  if (isnan(x)) return encode_exact(x, f);
+  float a = fabsf(x);
+  if (isinf(a) && !f->saturate) return encode_exact(x, f);
+  if (a > f->max) a = f->max;
+  float q, rem, ulp;
+  grid(a, f, &q, &rem, &ulp);
+  return encode_exact(copysignf(q * ulp, x), f);
+}
+
 /* One FP32 value rounded into storage `fmt` by `rule` (0 nearest, 1
- * stochastic) with hash counter `counter`; returns the stored bits.  FP32
- * rules are the identity (sr_states/rounding.py:127-136). */
+ * stochastic, 2 toward zero) with hash counter `counter`; returns the stored
+ * bits.  FP32 rules are the identity (sr_states/rounding.py:127-136). */
 uint32_t srs_o_round(float x, int fmt, int rule, uint32_t counter) {
   switch (fmt) {
     case FMT_F32: return f2u(x);
-    case FMT_BF16: return rule ? bf16_stochastic(x, counter) : bf16_nearest(x);
+    case FMT_BF16:
+      if (rule == 2) return bf16_toward_zero(x);
+      return rule ? bf16_stochastic(x, counter) : bf16_nearest(x);
     default: {
       const minifmt* f = minifmt_of(fmt);
+      if (rule == 2) return toward_zero_minifloat(x, f);
       return rule ? stochastic_minifloat(x, f, counter) : nearest_minifloat(x, f);
     }
   }

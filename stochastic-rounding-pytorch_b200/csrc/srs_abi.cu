@@ -68,7 +68,9 @@ int check_device() {
 }
 
 bool valid_format(int f) { return f >= SRS_FMT_F32 && f <= SRS_FMT_E5M2; }
-bool valid_rule(int r) { return r == SRS_RULE_NEAREST || r == SRS_RULE_STOCHASTIC; }
+bool valid_rule(int r) {
+  return r == SRS_RULE_NEAREST || r == SRS_RULE_STOCHASTIC || r == SRS_RULE_TOWARD_ZERO;
+}
 
 int check_hp_classes(int n) {
   if (n < 1 || n > SRS_MAX_STEP_CLASSES)
@@ -147,9 +149,12 @@ float numerator_floor(float nss) {
 // Per step class: the exact reciprocal of bias2_sqrt, the numerator range
 // [2^-59, 2^60) of the reciprocal division (empty unless 2^-30 <= c <= 2^30)
 // and whether the screened arithmetic path applies (2^-10 <= c <= 1,
-// |neg_step_size| <= 1, 0 <= eps <= 2^28; NaN scalars fail every test).
+// |neg_step_size| <= 1, 0 <= eps <= 2^28; NaN scalars fail every test).  A
+// toward-zero state rule also disables it: its stores run on the exact path.
+// Needs a.m_rule and a.v_rule set.
 void fill_reciprocals(const srs_adamw_hparams& hp, AdamWArgs& a) {
-  const bool eps_ok = hp.eps >= 0.0f && hp.eps <= 0x1p28f;
+  const bool screen_ok = hp.eps >= 0.0f && hp.eps <= 0x1p28f &&
+                         a.m_rule != SRS_RULE_TOWARD_ZERO && a.v_rule != SRS_RULE_TOWARD_ZERO;
   for (int c = 0; c < hp.n_step_classes; ++c) {
     const float b = hp.bias2_sqrt[c];
     a.inv_bias2_sqrt[c] = exact_reciprocal(b);
@@ -157,7 +162,7 @@ void fill_reciprocals(const srs_adamw_hparams& hp, AdamWArgs& a) {
     a.fast_lo[c] = ok ? 0x22000000u : 0u;
     a.fast_hi[c] = ok ? 0x5D800000u : 0u;
     const float nss = hp.neg_step_size[c];
-    a.fast_math[c] = (b >= 0x1p-10f && b <= 1.0f && nss >= -1.0f && nss <= 1.0f && eps_ok) ? 1 : 0;
+    a.fast_math[c] = (b >= 0x1p-10f && b <= 1.0f && nss >= -1.0f && nss <= 1.0f && screen_ok) ? 1 : 0;
     a.m_floor[c] = numerator_floor(nss);
   }
 }
@@ -298,10 +303,10 @@ static int adamw_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int
   a.tile_lo = tile_lo;
   a.tile_hi = tile_hi;
   a.hp = *hp;
-  fill_reciprocals(*hp, a);
   a.rng = *rng;
-  a.m_stochastic = m_rule;
-  a.v_stochastic = v_rule;
+  a.m_rule = m_rule;
+  a.v_rule = v_rule;
+  fill_reciprocals(*hp, a);
   if (peers != nullptr) a.peers = *peers;
   const cudaError_t e = kAdamW[m_format][v_format](rows, n_rows, n_tiles,
                                                    kind_index(uniform_kind), a, grid_ctas,
@@ -329,7 +334,7 @@ static int sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int 
   a.tile_hi = tile_hi;
   a.hp = *hp;
   a.rng = *rng;
-  a.u_stochastic = u_rule;
+  a.u_rule = u_rule;
   if (peers != nullptr) a.peers = *peers;
   const cudaError_t e = kSgdm[u_format](rows, n_rows, n_tiles, kind_index(uniform_kind), a,
                                         grid_ctas, static_cast<cudaStream_t>(stream));
@@ -482,10 +487,10 @@ int srs_adamw_single(const srs_row* row, int m_format, int m_rule, int v_format,
   a.tile_lo = 0;
   a.tile_hi = n_tiles;
   a.hp = *hp;
-  fill_reciprocals(*hp, a);
   a.rng.key_mode = SRS_KEY_GIVEN;
-  a.m_stochastic = m_rule;
-  a.v_stochastic = v_rule;
+  a.m_rule = m_rule;
+  a.v_rule = v_rule;
+  fill_reciprocals(*hp, a);
   const cudaError_t e = kAdamW[m_format][v_format](nullptr, 1, n_tiles, (int)(row->flags & 3u),
                                                    a, grid_ctas,
                                                    static_cast<cudaStream_t>(stream));
@@ -511,7 +516,7 @@ int srs_sgdm_single(const srs_row* row, int u_format, int u_rule, const srs_sgdm
   a.tile_hi = n_tiles;
   a.hp = *hp;
   a.rng.key_mode = SRS_KEY_GIVEN;
-  a.u_stochastic = u_rule;
+  a.u_rule = u_rule;
   const cudaError_t e = kSgdm[u_format](nullptr, 1, n_tiles, (int)(row->flags & 3u), a,
                                         grid_ctas, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SRS_OK : cuda_fail(e, "srs_sgdm_single launch");
@@ -645,10 +650,10 @@ extern "C" int srs_adamw_multi_noalloc(const srs_row* host_rows, int64_t n_rows,
   if (e != cudaSuccess) return cuda_fail(e, "srs_adamw_multi_noalloc row copy");
   AdamWArgs a{};
   a.hp = *hp;
-  fill_reciprocals(*hp, a);
   a.rng = *rng;
-  a.m_stochastic = m_rule;
-  a.v_stochastic = v_rule;
+  a.m_rule = m_rule;
+  a.v_rule = v_rule;
+  fill_reciprocals(*hp, a);
   a.tile_lo = 0;
   a.tile_hi = n_tiles;
   e = kAdamW[m_format][v_format](table, n_rows, n_tiles, kind_index(kind), a, grid_ctas, s);

@@ -4,7 +4,7 @@
 namespace srs {
 
 template <int OF>
-cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int stochastic,
+cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int rule,
                         int vec_ok, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
   const int64_t work = (n + kTile - 1) / kTile;
@@ -12,7 +12,7 @@ cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int s
   const int grid =
       grid_for(reinterpret_cast<const void*>(&cast_kernel<OF>), work, grid_ctas, &err, smem);
   if (err != cudaSuccess) return err;
-  cast_kernel<OF><<<grid, kThreads, smem, stream>>>(x, y, n, base, stochastic, vec_ok);
+  cast_kernel<OF><<<grid, kThreads, smem, stream>>>(x, y, n, base, rule, vec_ok);
   return cudaGetLastError();
 }
 

@@ -201,6 +201,41 @@ __device__ __forceinline__ uint32_t f16_stochastic(float x, uint32_t h) {
   return r | ((b >> 16) & 0x8000u);
 }
 
+// ------------------------------------------------------ round toward zero --
+//
+// The value of largest magnitude not above |x| in the format, sign kept:
+// truncation onto the same grid, i.e. the stochastic rule with a hash that
+// never rounds up (h = 0xFFFFFFFF is not below any 24-bit threshold << 8).
+// Overflow follows IEEE round-toward-zero where the format has infinities to
+// keep (BF16, FP16: finite values end at the largest finite value, +-Inf
+// stays infinite) and saturation for FP8 (+-Inf -> +-max finite).  NaN is
+// stored as the other rules store it.
+
+__device__ __forceinline__ uint32_t bf16_toward_zero(float x) {
+  return (x != x) ? 0xFFFFu : (__float_as_uint(x) >> 16);
+}
+
+__device__ __forceinline__ uint32_t e4m3_toward_zero(float x) { return e4m3_stochastic(x, ~0u); }
+
+__device__ __forceinline__ uint32_t e5m2_toward_zero(float x) { return e5m2_stochastic(x, ~0u); }
+
+__device__ __forceinline__ uint32_t f16_toward_zero(float x) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t u = b & 0x7FFFFFFFu;
+  if (u < 0x7F800000u) {  // finite: clamp to 65504 (0x477FE000) and truncate
+    return grid_stochastic_magnitude<10, 113>(min(u, 0x477FE000u), ~0u) | ((b >> 16) & 0x8000u);
+  }
+  return f16_stochastic(x, ~0u);  // +-Inf and NaN
+}
+
+template <int F>
+__device__ __forceinline__ uint32_t toward_zero1(float x) {
+  if constexpr (F == SRS_FMT_BF16) return bf16_toward_zero(x);
+  else if constexpr (F == SRS_FMT_F16) return f16_toward_zero(x);
+  else if constexpr (F == SRS_FMT_E4M3) return e4m3_toward_zero(x);
+  else return e5m2_toward_zero(x);
+}
+
 // ------------------------------------- stochastic rounding of screened vectors --
 //
 // Fast forms of the rules above for 8-element vectors that passed a screen (no
@@ -489,18 +524,36 @@ __device__ __forceinline__ void encode8_stochastic_fast(const float (&x)[kVec], 
   else encode8_stochastic_fast_as<F, false>(x, ctr0, 0u, w);
 }
 
-// Round 8 FP32 values into storage format F.  Element j of a stochastic rule
-// uses the hash of counter `ctr0 + j` (mod 2^32).  FP32 storage is the identity.
+// Round toward zero, 8 values, one element at a time.
 template <int F>
-__device__ __forceinline__ void encode8(const float (&x)[kVec], uint32_t ctr0, bool stochastic,
+__device__ __forceinline__ void encode8_toward_zero(const float (&x)[kVec],
+                                                 uint32_t (&w)[kWords<F>]) {
+  constexpr int kPerWord = kVec / kWords<F>;  // 2 (16-bit) or 4 (8-bit) per word
+#pragma unroll
+  for (int i = 0; i < kWords<F>; ++i) {
+    uint32_t word = 0u;
+#pragma unroll
+    for (int k = 0; k < kPerWord; ++k)
+      word |= toward_zero1<F>(x[kPerWord * i + k]) << ((32 / kPerWord) * k);
+    w[i] = word;
+  }
+}
+
+// Round 8 FP32 values into storage format F by `rule` (SRS_RULE_*).  Element j
+// of the stochastic rule uses the hash of counter `ctr0 + j` (mod 2^32).  FP32
+// storage is the identity under every rule.
+template <int F>
+__device__ __forceinline__ void encode8(const float (&x)[kVec], uint32_t ctr0, int rule,
                                         uint32_t (&w)[kWords<F>]) {
   if constexpr (F == SRS_FMT_F32) {
 #pragma unroll
     for (int j = 0; j < kVec; ++j) w[j] = __float_as_uint(x[j]);
-  } else if (stochastic) {
+  } else if (rule == SRS_RULE_STOCHASTIC) {
     const bool fast = (F == SRS_FMT_BF16) ? screen_bf16(x) : screen_grid(x);
     if (fast) encode8_stochastic_fast<F>(x, ctr0, w);
     else encode8_stochastic_exact<F>(x, ctr0, w);
+  } else if (rule == SRS_RULE_TOWARD_ZERO) {
+    encode8_toward_zero<F>(x, w);
   } else if constexpr (F == SRS_FMT_BF16 || F == SRS_FMT_F16) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -556,7 +609,7 @@ __device__ __forceinline__ void store_param8(void* base, int64_t e0, int count, 
                                              const srs_peers* peers = nullptr) {
   constexpr int F = BF16 ? SRS_FMT_BF16 : SRS_FMT_F32;
   uint32_t w[kWords<F>];
-  encode8<F>(x, 0u, false, w);
+  encode8<F>(x, 0u, SRS_RULE_NEAREST, w);
   if (vec) store_raw8<F>(base, e0, w);
   else store_raw_partial<F>(base, e0, count, w);
   if (peers != nullptr) {
@@ -581,26 +634,27 @@ __device__ __forceinline__ void load_state8(const void* base, int64_t e0, int co
 template <int F>
 __device__ __forceinline__ void store_state8(void* base, int64_t e0, int count, bool vec,
                                              const float (&x)[kVec], uint32_t ctr0,
-                                             bool stochastic) {
+                                             int rule) {
   uint32_t w[kWords<F>];
-  encode8<F>(x, ctr0, stochastic, w);
+  encode8<F>(x, ctr0, rule, w);
   if (vec) store_raw8<F>(base, e0, w);
   else store_raw_partial<F>(base, e0, count, w);
 }
 
 // store_state8 for values known to pass the screen of their format (no NaN;
 // for the FP16/FP8 grids |x| < 2^63): the stochastic rule goes straight to the
-// fast form.
+// fast form.  Only the stochastic and nearest rules come here (toward-zero
+// states take store_state8), which keeps the hot loops free of that code.
 template <int F>
 __device__ __forceinline__ void store_state8_screened(void* base, int64_t e0, int count, bool vec,
                                                       const float (&x)[kVec], uint32_t ctr0,
                                                       bool stochastic) {
   uint32_t w[kWords<F>];
   if constexpr (F == SRS_FMT_F32) {
-    encode8<F>(x, ctr0, false, w);
+    encode8<F>(x, ctr0, SRS_RULE_NEAREST, w);
   } else {
     if (stochastic) encode8_stochastic_fast<F>(x, ctr0, w);
-    else encode8<F>(x, ctr0, false, w);
+    else encode8<F>(x, ctr0, SRS_RULE_NEAREST, w);
   }
   if (vec) store_raw8<F>(base, e0, w);
   else store_raw_partial<F>(base, e0, count, w);

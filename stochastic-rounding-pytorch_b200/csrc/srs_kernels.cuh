@@ -35,8 +35,8 @@ struct AdamWArgs {
   // Smallest |m'| whose numerator nss*m' is >= 2^-90 (Inf when nss == 0).
   float m_floor[SRS_MAX_STEP_CLASSES];
   srs_rng rng;
-  int32_t m_stochastic;
-  int32_t v_stochastic;
+  int32_t m_rule;  // SRS_RULE_* of the stored first moment
+  int32_t v_rule;  // SRS_RULE_* of the stored second moment
   srs_peers peers;  // replicas that receive the updated parameters (n_peers == 0: none)
   int64_t tile_lo, tile_hi;  // the launch covers tiles [tile_lo, tile_hi) of the table
 };
@@ -45,7 +45,7 @@ struct SgdmArgs {
   srs_row inline_row;  // the single row of srs_sgdm_single (rows == nullptr)
   srs_sgdm_hparams hp;
   srs_rng rng;
-  int32_t u_stochastic;
+  int32_t u_rule;  // SRS_RULE_* of the stored momentum
   srs_peers peers;
   int64_t tile_lo, tile_hi;
 };
@@ -390,8 +390,8 @@ __device__ __noinline__ void adamw8_exact(const RowView& rv, int64_t e0, int cou
   }
   const uint32_t ctr_m = (uint32_t)e0 + rv.ctr0, ctr_v = (uint32_t)e0 + rv.ctr1;
   store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
-  store_state8<MF>(rv.s0, e0, count, VEC, m, ctr_m, a.m_stochastic != 0);
-  store_state8<VF>(rv.s1, e0, count, VEC, v, ctr_v, a.v_stochastic != 0);
+  store_state8<MF>(rv.s0, e0, count, VEC, m, ctr_m, a.m_rule);
+  store_state8<VF>(rv.s1, e0, count, VEC, v, ctr_v, a.v_rule);
 }
 
 // Moments, screen and update of one thread's 8 loaded elements, then the
@@ -421,8 +421,10 @@ __device__ __forceinline__ void adamw8_compute(const RowView& rv, int64_t e0, in
       adamw_update_fast(p, m, v, y, k, a);
       const uint32_t ctr_m = (uint32_t)e0 + rv.ctr0, ctr_v = (uint32_t)e0 + rv.ctr1;
       store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
-      store_state8_screened<MF>(rv.s0, e0, count, VEC, m, ctr_m, a.m_stochastic != 0);
-      store_state8_screened<VF>(rv.s1, e0, count, VEC, v, ctr_v, a.v_stochastic != 0);
+      store_state8_screened<MF>(rv.s0, e0, count, VEC, m, ctr_m,
+                                a.m_rule == SRS_RULE_STOCHASTIC);
+      store_state8_screened<VF>(rv.s1, e0, count, VEC, v, ctr_v,
+                                a.v_rule == SRS_RULE_STOCHASTIC);
       return;
     }
   }
@@ -569,7 +571,7 @@ __device__ __forceinline__ void sgdm8_compute(const RowView& rv, int64_t e0, int
     u[2 * i + 1] = u1.y;
   }
   store_param8<PB>(rv.p, e0, count, VEC, p, &a.peers);
-  store_state8<UF>(rv.s0, e0, count, VEC, u, (uint32_t)e0 + rv.ctr0, a.u_stochastic != 0);
+  store_state8<UF>(rv.s0, e0, count, VEC, u, (uint32_t)e0 + rv.ctr0, a.u_rule);
 }
 
 template <bool PB, bool GB, int UF, bool VEC>
@@ -662,29 +664,40 @@ __global__ void __launch_bounds__(kThreads)
 
 // ----------------------------------------------------------------- cast --
 
-// y[e] = round(x[e]); stochastic counter (e + base) mod 2^32 with base = seed + offset.
-// Round to nearest is a plain copy-like stream: a grid-stride loop of 8-element
-// vectors reaches the copy bandwidth.  The stochastic rules do more arithmetic
+// y[e] = round(x[e]) by `rule`; stochastic counter (e + base) mod 2^32 with
+// base = seed + offset.
+// Round to nearest (and toward zero) is a plain copy-like stream: a grid-stride
+// loop of 8-element vectors reaches the copy bandwidth.  The stochastic rules do more arithmetic
 // per byte: each CTA takes a contiguous range of 2048-element tiles and, with
 // aligned input and output (vec_ok), double-buffers full tiles through shared
 // memory by per-thread cp.async copies of the thread's 32 input bytes, so the
 // loads of the next tile are in flight during the hashing and rounding.
 constexpr int kCastStageBytes = kThreads * kVec * 4;  // one tile of FP32 input
 
+template <int OF, int RULE>
+__device__ __forceinline__ void cast_grid_stride(const float* __restrict__ x, void* __restrict__ y,
+                                                 int64_t n, int vec_ok) {
+  const int64_t stride = (int64_t)gridDim.x * kThreads * kVec;
+  for (int64_t e0 = ((int64_t)blockIdx.x * kThreads + threadIdx.x) * kVec; e0 < n;
+       e0 += stride) {
+    const int count = (int)min((int64_t)kVec, n - e0);
+    const bool vec = vec_ok != 0 && count == kVec;
+    float v[kVec];
+    load_state8<SRS_FMT_F32>(x, e0, count, vec, v);
+    store_state8<OF>(y, e0, count, vec, v, 0u, RULE);
+  }
+}
+
 template <int OF>
 __global__ void __launch_bounds__(kThreads)
     cast_kernel(const float* __restrict__ x, void* __restrict__ y, int64_t n, uint32_t base,
-                int stochastic, int vec_ok) {
-  if (!stochastic) {
-    const int64_t stride = (int64_t)gridDim.x * kThreads * kVec;
-    for (int64_t e0 = ((int64_t)blockIdx.x * kThreads + threadIdx.x) * kVec; e0 < n;
-         e0 += stride) {
-      const int count = (int)min((int64_t)kVec, n - e0);
-      const bool vec = vec_ok != 0 && count == kVec;
-      float v[kVec];
-      load_state8<SRS_FMT_F32>(x, e0, count, vec, v);
-      store_state8<OF>(y, e0, count, vec, v, 0u, false);
-    }
+                int rule, int vec_ok) {
+  if (rule == SRS_RULE_NEAREST) {
+    cast_grid_stride<OF, SRS_RULE_NEAREST>(x, y, n, vec_ok);
+    return;
+  }
+  if (rule == SRS_RULE_TOWARD_ZERO) {
+    cast_grid_stride<OF, SRS_RULE_TOWARD_ZERO>(x, y, n, vec_ok);
     return;
   }
   extern __shared__ __align__(16) char stage_mem[];
@@ -709,7 +722,7 @@ __global__ void __launch_bounds__(kThreads)
       const float v[kVec] = {__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z),
                              __uint_as_float(a.w), __uint_as_float(b.x), __uint_as_float(b.y),
                              __uint_as_float(b.z), __uint_as_float(b.w)};
-      store_state8<OF>(y, e0, kVec, true, v, base + (uint32_t)e0, true);
+      store_state8<OF>(y, e0, kVec, true, v, base + (uint32_t)e0, SRS_RULE_STOCHASTIC);
     }
     tile += n_full;
   }
@@ -719,7 +732,7 @@ __global__ void __launch_bounds__(kThreads)
       const bool vec = vec_ok != 0 && count == kVec;
       float v[kVec];
       load_state8<SRS_FMT_F32>(x, e0, count, vec, v);
-      store_state8<OF>(y, e0, count, vec, v, base + (uint32_t)e0, true);
+      store_state8<OF>(y, e0, count, vec, v, base + (uint32_t)e0, SRS_RULE_STOCHASTIC);
     }
   }
 }
@@ -756,7 +769,7 @@ cudaError_t launch_sgdm(const srs_row* rows, int64_t n_rows, int64_t n_tiles, in
                         const SgdmArgs& a, int grid_ctas, cudaStream_t stream);
 
 template <int OF>
-cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int stochastic,
+cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int rule,
                         int vec_ok, int grid_ctas, cudaStream_t stream);
 
 }  // namespace srs

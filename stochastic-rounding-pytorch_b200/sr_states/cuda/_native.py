@@ -123,7 +123,7 @@ _SIGNATURES = {
     "srs_ipc_close": ([_P], ctypes.c_int),
 }
 NOALLOC_MAX_ROWS = 4096
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _lock = threading.Lock()
 _library = None

@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import torch
 
-from ..rounding import native_codes, validate_rounding
+from ..rounding import NATIVE_RULES, native_codes, native_format, validate_rounding
 from . import _native
 from ._launch import device_guard, stream_handle
 from ._validate import CAST_BLOCK_SIZES, CAST_NUM_WARPS, CAST_STORE_MODES
@@ -75,10 +75,11 @@ def rn_cast_bf16(x, *, block_size=256, num_warps=4):
 
 
 def cast_any_layout(x, *, dtype, rule, seed, offset):
-    """Built-in rule of ``sr_states.cast``: any shape/strides, counters in
-    row-major order of the logical tensor, output shaped like ``x``."""
+    """Device rule ``rule`` (a name of NATIVE_RULES) of ``sr_states.cast``: any
+    shape/strides, counters in row-major order of the logical tensor, output
+    shaped like ``x``."""
     _native.launcher().check_device(x.device, "the built-in rounding rules (sm_100a kernels)")
-    fmt, code = native_codes(dtype, rule)
+    fmt, code = native_format(dtype), NATIVE_RULES.index(rule)
     src = x.contiguous()
     out = torch.empty(x.shape, dtype=dtype, device=x.device)
     return _launch(src, out, fmt, code, seed, offset)

@@ -5,6 +5,14 @@ Public surface of the reference (sr_states/rounding.py:28-124): ``register_round
 messages.  The built-in rules (nearest and stochastic for FP32, BF16, FP16,
 FP8 E4M3/E5M2) execute on the sm_100a kernels of ``libsrs_b200.so``.
 
+Custom rules: the reference runs a custom rule in its fused kernels through a
+``@triton.jit`` callback (sr_states/rounding.py:28-66).  Here the kernels hold
+a small table of device rules selected by id (``NATIVE_RULES``, the
+``SRS_RULE_*`` codes of include/srs_b200.h): nearest, stochastic and
+toward_zero.  ``register_rounding(..., native=<id>)`` binds a name to one of
+them; ``native_reference(<id>)`` is the kernel-backed callable of that rule,
+for registrations without a CPU implementation of their own.
+
 Backends named in validation:
   ``"reference"`` (also ``"compiled"``): any registered rule; ``cast`` calls the
       rule's ``reference`` callable (the built-ins' callable is the native kernel).
@@ -20,7 +28,10 @@ from dataclasses import dataclass
 
 import torch
 
-NATIVE_RULES = ("nearest", "stochastic")
+# Device rules by SRS_RULE_* code.  Only the first two are built-in names;
+# "toward_zero" is reachable through register_rounding(..., native=...).
+NATIVE_RULES = ("nearest", "stochastic", "toward_zero")
+_BUILTIN_RULES = NATIVE_RULES[:2]
 _BACKENDS = {"reference": None, "compiled": None, "cuda": "CUDA", "triton": "Triton"}
 
 
@@ -48,9 +59,11 @@ def register_rounding(
     a tensor of ``dtype`` with the same shape and device, without mutating x;
     ``sr_states.cast`` and the per-parameter ``StateOptimizer`` path call it.
 
-    ``native`` names the built-in sm_100a rule ("nearest" or "stochastic") that
-    the fused optimizers run for this name; rules without one are rejected by
-    the fused optimizers.  ``triton`` (a ``@triton.jit`` callback in the
+    ``native`` names the sm_100a device rule ("nearest", "stochastic" or
+    "toward_zero": the format's value of largest magnitude not above |x|, sign
+    kept) that the fused optimizers run for this name; rules without one are
+    rejected by the fused optimizers.  The caller vouches that ``reference``
+    and the device rule agree.  ``triton`` (a ``@triton.jit`` callback in the
     reference) is accepted so registrations keep importing, but no Triton code
     runs here.  Names and dtypes are stored in checkpoints, callables are not;
     an existing registration can never be replaced.
@@ -95,6 +108,13 @@ _NATIVE_FORMATS = {
 }
 
 
+def native_format(dtype: torch.dtype) -> int:
+    """SRS_FMT_* code of a storage dtype the kernels support."""
+    if dtype not in _NATIVE_FORMATS:
+        raise ValueError(f"no native kernels store {dtype}")
+    return _NATIVE_FORMATS[dtype]
+
+
 def native_codes(dtype: torch.dtype, rounding: str) -> tuple[int, int]:
     """(SRS_FMT_*, SRS_RULE_*) of a rule usable by the fused kernels."""
     validate_rounding(dtype, rounding, backend="cuda")
@@ -131,10 +151,20 @@ def cast(
     return result
 
 
-def _builtin(rule: str) -> Callable:
+def native_reference(rule: str) -> Callable:
+    """The ``reference`` callable of device rule ``rule`` (one of NATIVE_RULES):
+    ``(x, *, dtype, seed, offset) -> Tensor`` running the sm_100a cast kernel
+    (any shape and strides, counters in row-major order; FP32 is the identity).
+    Register it together with ``native=rule`` to use a device rule under a
+    name of your own."""
+    if rule not in NATIVE_RULES:
+        raise ValueError(f"rule must be one of {NATIVE_RULES}")
+
     def run(x, *, dtype, seed, offset):
         if dtype == torch.float32:
             return x.to(torch.float32)
+        if dtype not in _NATIVE_FORMATS:
+            raise ValueError(f"no native kernels store {dtype}")
         from .cuda.cast import cast_any_layout
 
         return cast_any_layout(x, dtype=dtype, rule=rule, seed=seed, offset=offset)
@@ -144,6 +174,6 @@ def _builtin(rule: str) -> Callable:
 
 
 for _dtype in _NATIVE_FORMATS:
-    for _rule in NATIVE_RULES:
-        _RULES[_dtype, _rule] = _Rule(_builtin(_rule), _rule)
+    for _rule in _BUILTIN_RULES:
+        _RULES[_dtype, _rule] = _Rule(native_reference(_rule), _rule)
 del _dtype, _rule

@@ -73,7 +73,7 @@ int main(void) {{
 
 def test_library_information_without_a_gpu():
     lib = _native.load_library()
-    assert lib.srs_abi_version() == 4
+    assert lib.srs_abi_version() == 5
     assert lib.srs_tile_elems() == 2048
 
 
