@@ -201,19 +201,20 @@ def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunk
     gen = torch.Generator(device=device).manual_seed(7)
     flat_p = torch.empty(total, dtype=torch.bfloat16, device=device).normal_(0, 0.02,
                                                                               generator=gen)
-    flat_g = torch.empty(total, dtype=torch.bfloat16, device=device).normal_(0, 1e-4,
-                                                                              generator=gen)
     params, offset = [], 0
     for shape in shapes:
         n = math.prod(shape)
-        p = torch.nn.Parameter(flat_p[offset:offset + n].view(shape))
-        p.grad = flat_g[offset:offset + n].view(shape)
-        params.append(p)
+        params.append(torch.nn.Parameter(flat_p[offset:offset + n].view(shape)))
         offset += n
     fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn, "stochastic"),
            "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
+    # Flat gradient buffers (every p.grad a view into them): the layout the
+    # host-streamed step of the e2e measurement loads into.
     opt = ZeroAdamW(params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1,
-                    state_format=fmt, seed=7, gather=gather, chunks=chunks)
+                    state_format=fmt, seed=7, gather=gather, chunks=chunks,
+                    grads="reduce_scatter")
+    flat_g = opt.flat_grads(torch.bfloat16)
+    flat_g.normal_(0, 1e-4, generator=gen)
     return opt, params, flat_p, flat_g, total
 
 
@@ -278,30 +279,32 @@ def cpu_baseline(seconds):
 
 
 def e2e_run(opt, flat_p, flat_g, steps, world, total):
-    """The step through the public API with host buffers: per step the BF16
-    gradients come from pinned host memory and the updated BF16 parameters go
-    back to it (the optimizer states stay on the device)."""
+    """The step through the public API with host buffers (``ZeroAdamW.step_host``):
+    per step each rank's BF16 gradient shard comes from pinned host memory and
+    its updated BF16 parameter shard goes back to it, both streamed in tile
+    chunks alongside the update (the optimizer states stay on the device)."""
     import torch
 
-    shard = flat_g.numel()
-    host_g = torch.empty(shard, dtype=torch.bfloat16, pin_memory=True)
-    host_p = torch.empty(flat_p.numel(), dtype=torch.bfloat16, pin_memory=True)
-    host_g.copy_(flat_g)
+    n = opt.flat_numel(torch.bfloat16)
+    host_g = torch.empty(n, dtype=torch.bfloat16, pin_memory=True)
+    host_p = torch.empty(n, dtype=torch.bfloat16, pin_memory=True)
+    host_g.copy_(flat_g[:n])
+    shard = opt.local_numel()  # this rank's elements: what each copy moves
+    opt.step_host(host_g, host_p)  # warm-up: streams and the chunk plan
     stream = torch.cuda.current_stream()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for _ in range(steps):
-        flat_g.copy_(host_g, non_blocking=True)
-        opt.step()
-        host_p.copy_(flat_p, non_blocking=True)
+        opt.step_host(host_g, host_p)
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
     return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms,
-            "h2d_bytes_per_step": host_g.numel() * 2, "d2h_bytes_per_step": host_p.numel() * 2}
+            "h2d_bytes_per_step": shard * 2, "d2h_bytes_per_step": shard * 2,
+            "api": "ZeroAdamW.step_host (pinned host gradients in, parameters out)"}
 
 
 def run_b200(args):

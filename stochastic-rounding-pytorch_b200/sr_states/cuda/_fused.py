@@ -117,14 +117,17 @@ def adamw_group_step(optimizer, group, formats, items, rng_step) -> None:
                            launch.steps)
         exchange = getattr(optimizer, "_srs_exchange", None)
         with torch.cuda.device(launch.device) if launch.device.type == "cuda" else _null():
-            if exchange is not None:
-                exchange.run(launch, lambda lo, hi, launch=launch, hp=hp: launcher.adamw_multi(
-                    launch.table, launch.table.n_rows, launch.table.n_tiles, m_fmt, m_rule,
-                    v_fmt, v_rule, hp, rng, _stream(launch.device), tiles=(lo, hi)))
-            else:
+            def whole(launch=launch, hp=hp):
                 launcher.adamw_multi(launch.table, launch.table.n_rows, launch.table.n_tiles,
                                      m_fmt, m_rule, v_fmt, v_rule, hp, rng,
                                      _stream(launch.device), **_peers_of(optimizer))
+
+            if exchange is not None:
+                exchange.run(launch, lambda lo, hi, launch=launch, hp=hp: launcher.adamw_multi(
+                    launch.table, launch.table.n_rows, launch.table.n_tiles, m_fmt, m_rule,
+                    v_fmt, v_rule, hp, rng, _stream(launch.device), tiles=(lo, hi)), whole)
+            else:
+                whole()
     if steps is None:
         for _, state, _, step, _ in items:
             state["step"] = step
@@ -154,14 +157,17 @@ def sgdm_group_step(optimizer, group, formats, items, rng_step) -> None:
     for launch in launches:
         exchange = getattr(optimizer, "_srs_exchange", None)
         with torch.cuda.device(launch.device) if launch.device.type == "cuda" else _null():
-            if exchange is not None:
-                exchange.run(launch, lambda lo, hi, launch=launch: launcher.sgdm_multi(
-                    launch.table, launch.table.n_rows, launch.table.n_tiles, u_fmt, u_rule, hp,
-                    rng, _stream(launch.device), tiles=(lo, hi)))
-            else:
+            def whole(launch=launch):
                 launcher.sgdm_multi(launch.table, launch.table.n_rows, launch.table.n_tiles,
                                     u_fmt, u_rule, hp, rng, _stream(launch.device),
                                     **_peers_of(optimizer))
+
+            if exchange is not None:
+                exchange.run(launch, lambda lo, hi, launch=launch: launcher.sgdm_multi(
+                    launch.table, launch.table.n_rows, launch.table.n_tiles, u_fmt, u_rule, hp,
+                    rng, _stream(launch.device), tiles=(lo, hi)), whole)
+            else:
+                whole()
     if fresh:
         _remember(cache, optimizer, group, formats, launches, items, False)
 

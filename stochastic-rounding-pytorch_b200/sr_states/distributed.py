@@ -78,8 +78,10 @@ class FlatLayout:
         by_dtype: dict[torch.dtype, list] = {}
         for p in params:
             by_dtype.setdefault(p.dtype, []).append(p)
+        self.numel: dict[torch.dtype, int] = {}  # parameter elements (unpadded) per dtype
         for dtype, plist in by_dtype.items():
             total = sum(p.numel() for p in plist)
+            self.numel[dtype] = total
             unit = world * SHARD_ALIGN
             padded = -(-total // unit) * unit
             buffer = self._adopt(plist, padded)
@@ -126,27 +128,47 @@ class FlatLayout:
         return (lo, hi) if lo < hi else None
 
 
-class _ChunkedExchange:
-    """Pipelined parameter exchange of a sharded step (``gather="copy"``): each
-    launch of the step runs over ``chunks`` consecutive tile ranges of its row
-    table, and after each range the copy engines send the range's updated
-    parameters to every peer (one stream per peer, device-to-device copies into
-    the peers' mapped buffers) while the next range is updated.  A tile range
-    covers one contiguous run of the flat buffer per parameter dtype, because
-    the rows follow the flat buffer's order."""
+class _HostIO:
+    """The pinned host buffers of one ``step_host`` call."""
 
-    def __init__(self, layout, peer_starts, device, chunks=32):
+    __slots__ = ("grads", "params", "grad_buffers")
+
+    def __init__(self, grads, params, grad_buffers):
+        self.grads, self.params, self.grad_buffers = grads, params, grad_buffers
+
+
+class _ChunkedExchange:
+    """Pipelined copies around a sharded step.  Each launch of the step runs over
+    ``chunks`` consecutive tile ranges of its row table, and after each range
+    the copy engines move the range's updated parameters while the next range
+    is updated:
+
+    * ``gather="copy"``: to every peer (one stream per peer, device-to-device
+      copies into the peers' mapped buffers);
+    * ``step_host``: to pinned host memory (one device-to-host stream), while a
+      host-to-device stream loads each range's gradients ahead of its launch.
+
+    A tile range covers one contiguous run of the flat buffer per parameter
+    dtype, because the rows follow the flat buffer's order.  ``chunks=1``
+    with ``whole=True`` keeps one full launch (the fused peer stores need it)
+    and only brackets it with the host copies."""
+
+    def __init__(self, layout, peer_starts, device, chunks=32, whole=False):
         self._layout = layout
-        self._peer_starts = peer_starts  # dtype -> start of each peer's buffer, here
-        self._chunks = chunks
-        n_peers = len(next(iter(peer_starts.values())))
+        self._peer_starts = peer_starts or {}  # dtype -> start of each peer's buffer, here
+        self._chunks = 1 if whole else chunks
+        self._whole = whole
+        n_peers = len(next(iter(peer_starts.values()))) if peer_starts else 0
         self._streams = [torch.cuda.Stream(device) for _ in range(n_peers)]
+        self._device = device
+        self._host_streams = None
+        self.host: _HostIO | None = None  # set for the duration of a step_host call
 
     def _plan(self, table):
         """[(tile_lo, tile_hi, [(dtype, address, bytes), ...]), ...] for a table."""
-        plan = getattr(table, "_srs_exchange_plan", None)
-        if plan is not None:
-            return plan
+        cached = getattr(table, "_srs_exchange_plan", None)
+        if cached is not None and cached[0] == self._chunks:
+            return cached[1]
         from .cuda import _native
 
         host, tile = table.host, 2048
@@ -172,18 +194,50 @@ class _ChunkedExchange:
                 else:
                     runs.append((dtype, start, nbytes))
             plan.append((lo, hi, runs))
-        table._srs_exchange_plan = plan
+        table._srs_exchange_plan = (self._chunks, plan)
         return plan
 
-    def run(self, launch, launch_tiles):
+    def _flat(self, dtype, start, nbytes):
+        """[a, b) flat element range of a run of the dtype's parameter buffer."""
+        buffer = self._layout.buffers[dtype]
+        size = buffer.element_size()
+        a = (start - buffer.data_ptr()) // size
+        return a, a + nbytes // size
+
+    def run(self, launch, launch_tiles, launch_whole=None):
         """launch_tiles(lo, hi) enqueues the step over tiles [lo, hi) on the
-        current stream."""
+        current stream; launch_whole() the full launch (``whole=True``)."""
         from .cuda import _native
 
         launcher = _native.launcher()
         compute = torch.cuda.current_stream(launch.device)
-        for lo, hi, runs in self._plan(launch.table):
-            launch_tiles(lo, hi)
+        plan = self._plan(launch.table)
+        host = self.host
+        loaded = []
+        if host is not None:
+            if self._host_streams is None:
+                self._host_streams = (torch.cuda.Stream(self._device),
+                                      torch.cuda.Stream(self._device))
+            h2d, d2h = self._host_streams
+            # Gradient loads overwrite what earlier work on the stream may read.
+            h2d.wait_stream(compute)
+            d2h.wait_stream(compute)
+            with torch.cuda.stream(h2d):
+                for _, _, runs in plan:
+                    for dtype, start, nbytes in runs:
+                        a, b = self._flat(dtype, start, nbytes)
+                        host.grad_buffers[dtype][a:b].copy_(host.grads[dtype][a:b],
+                                                            non_blocking=True)
+                    event = torch.cuda.Event()
+                    event.record(h2d)
+                    loaded.append(event)
+        for i, (lo, hi, runs) in enumerate(plan):
+            if loaded:
+                compute.wait_event(loaded[i])
+            if self._whole:
+                launch_whole()
+            else:
+                launch_tiles(lo, hi)
             done = torch.cuda.Event()
             done.record(compute)
             for w, stream in enumerate(self._streams):
@@ -192,8 +246,17 @@ class _ChunkedExchange:
                     local = self._layout.buffers[dtype].data_ptr()
                     launcher.copy_async(self._peer_starts[dtype][w] + (start - local), start,
                                         nbytes, stream.cuda_stream)
+            if host is not None and host.params is not None:
+                d2h.wait_event(done)
+                with torch.cuda.stream(d2h):
+                    for dtype, start, nbytes in runs:
+                        a, b = self._flat(dtype, start, nbytes)
+                        host.params[dtype][a:b].copy_(self._layout.buffers[dtype][a:b],
+                                                      non_blocking=True)
         for stream in self._streams:
             compute.wait_stream(stream)
+        if host is not None:
+            compute.wait_stream(self._host_streams[1])
 
 
 class _ZeroMixin:
@@ -223,6 +286,8 @@ class _ZeroMixin:
         self._peer_bases: list[int] = []
         self._srs_peers = None
         self._srs_exchange = None
+        self._host_pipeline = None
+        self._chunks = chunks
         self._sync = None
         if self._world > 1:
             device = next(iter(self._layout.buffers.values())).device
@@ -239,16 +304,18 @@ class _ZeroMixin:
                 elif connected is not None:
                     self._srs_exchange = _ChunkedExchange(self._layout, connected[1], device,
                                                           chunks)
+        if self._world == 1:
+            self._gather = "none"
+        elif self._srs_peers is not None:
+            self._gather = "fused"
+        else:
+            self._gather = "copy" if self._srs_exchange is not None else "nccl"
 
     @property
     def gather_mode(self) -> str:
         """'fused' (peer stores inside the step), 'copy' (copy engines pipelined
         with the step), 'nccl' (all-gather after it) or 'none' (one rank)."""
-        if self._world == 1:
-            return "none"
-        if self._srs_peers is not None:
-            return "fused"
-        return "copy" if self._srs_exchange is not None else "nccl"
+        return self._gather
 
     def _agree(self, value):
         """Every rank's ``value`` (a collective: all ranks call it together)."""
@@ -485,7 +552,7 @@ class _ZeroMixin:
     def step(self, closure=None):
         stream = torch.cuda.current_stream() if torch.cuda.is_available() else None
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if stream else None
-        fused = self._srs_peers is not None or self._srs_exchange is not None
+        fused = self._gather in ("fused", "copy")
         if marks:
             marks[0].record(stream)
         if fused:
@@ -507,6 +574,76 @@ class _ZeroMixin:
             marks[3].record(stream)
             self._events.append(marks)
         return loss
+
+    def flat_grads(self, dtype):
+        """The flat gradient buffer of a parameter dtype (``grads="reduce_scatter"``;
+        None otherwise): element i is the gradient of flat parameter element i."""
+        return self._grad_buffers.get(dtype)
+
+    def flat_numel(self, dtype) -> int:
+        """Parameter elements of a dtype, all ranks (the unpadded flat length)."""
+        return self._layout.numel[dtype]
+
+    @torch.no_grad()
+    def step_host(self, grads, params=None):
+        """One step whose gradients come from pinned host memory and whose updated
+        parameters go back to it, the copies pipelined with the update: the step
+        runs over ``chunks`` tile ranges, a host-to-device stream loads each
+        range's gradients ahead of its launch and a device-to-host stream sends
+        each finished range back, so both directions of PCIe and the kernel work
+        at the same time.  (With ``gather="fused"`` and more than one rank the
+        update stays one launch, bracketed by the two copies.)
+
+        ``grads`` / ``params``: {dtype: pinned CPU tensor} (a tensor alone when
+        all parameters share one dtype), laid out like the flat parameter
+        buffer of that dtype: element i belongs to flat element i, parameters in
+        optimizer order, back to back.  Each rank loads only its shard's
+        gradients and writes back only its shard's parameters.  Needs
+        ``grads="reduce_scatter"`` (the gradients are loaded into the flat
+        gradient buffers the parameters' ``.grad`` views).  The host buffers
+        are in use until the current stream has passed the step.
+        """
+        if not self._grad_buffers:
+            raise RuntimeError("step_host requires grads='reduce_scatter' (flat gradient buffers)")
+        grads = self._host_tensors(grads, "grads")
+        params = None if params is None else self._host_tensors(params, "params")
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p.grad is None or p.grad.data_ptr() != self._grad_slot(p).data_ptr():
+                    raise RuntimeError("step_host: every p.grad must be its flat gradient view "
+                                       "(set by the optimizer and zero_grad())")
+        pipeline = self._srs_exchange
+        restore = pipeline
+        if pipeline is None:
+            if self._host_pipeline is None:
+                device = next(iter(self._layout.buffers.values())).device
+                self._host_pipeline = _ChunkedExchange(self._layout, None, device, self._chunks,
+                                                       whole=self._srs_peers is not None)
+            pipeline = self._srs_exchange = self._host_pipeline
+        pipeline.host = _HostIO(grads, params, self._grad_buffers)
+        try:
+            return self.step()
+        finally:
+            pipeline.host = None
+            self._srs_exchange = restore
+
+    def _host_tensors(self, tensors, what):
+        if isinstance(tensors, torch.Tensor):
+            if len(self._layout.buffers) != 1:
+                raise ValueError(f"{what}: one tensor per parameter dtype is needed")
+            tensors = {next(iter(self._layout.buffers)): tensors}
+        out = {}
+        for dtype, buffer in self._layout.buffers.items():
+            t = tensors.get(dtype) if isinstance(tensors, dict) else None
+            if t is None:
+                raise ValueError(f"{what}: no host tensor for {dtype}")
+            need = self._layout.numel[dtype]
+            if (t.device.type != "cpu" or t.dtype != dtype or not t.is_contiguous()
+                    or t.dim() != 1 or t.numel() < need or not t.is_pinned()):
+                raise ValueError(f"{what}[{dtype}] must be a contiguous pinned 1-D CPU tensor of "
+                                 f"{dtype} with at least {need} elements")
+            out[dtype] = t
+        return out
 
     @property
     def timings(self):
@@ -531,6 +668,9 @@ class _ZeroMixin:
         self._close_peers()
         self._srs_peers = None
         self._srs_exchange = None
+        self._host_pipeline = None
+        if self._gather in ("fused", "copy"):
+            self._gather = "nccl"  # a later step all-gathers
 
 
 class _TimingList(list):

@@ -209,6 +209,31 @@ def _two_rank_worker(rank, world, port, results):
             if mode == "rs":
                 opt.close()
         same["reduce_scatter"] = all(np.array_equal(a, b) for a, b in zip(outs["rs"], outs["single"]))
+        # step_host in every gather mode: each rank loads its gradient shard from
+        # the host and writes back its parameter shard; the replicas equal the
+        # unsharded steps of the first block.
+        for mode in ("fused", "copy", "nccl"):
+            gen = torch.Generator().manual_seed(5)
+            params, grads = [], []
+            for n in SIZES:
+                params.append(torch.nn.Parameter(torch.randn(n, generator=gen)
+                                                 .to("cuda", torch.bfloat16)))
+                grads.append((torch.randn(n, generator=gen) * 1e-2).to(torch.bfloat16))
+            opt = ZeroAdamW(params, lr=1e-3, state_format=fmt, seed=9, gather=mode,
+                            grads="reduce_scatter")
+            host_g = torch.cat(grads).pin_memory()
+            host_p = torch.zeros(host_g.numel(), dtype=torch.bfloat16, pin_memory=True)
+            for _ in range(3):
+                opt.step_host(host_g, host_p)
+            torch.cuda.synchronize()
+            ok = all(np.array_equal(p.detach().view(torch.uint16).cpu().numpy(), b)
+                     for p, b in zip(params, runs["single"]))
+            lo, hi = opt._layout.shard(torch.bfloat16)
+            hi = min(hi, host_g.numel())
+            device = torch.cat([p.detach().reshape(-1) for p in params])
+            ok = ok and torch.equal(host_p[lo:hi], device[lo:hi].cpu())
+            same["host_" + mode] = ok
+            opt.close()
         results[rank] = ((runs["fused_mode"], runs["copy_mode"], runs["nccl_mode"]), same)
     finally:
         dist.destroy_process_group()
@@ -224,4 +249,5 @@ def test_two_ranks_fused_and_copy_gathers_equal_nccl_and_unsharded_steps():
     for rank in range(2):
         modes, same = results[rank]
         assert modes == ("fused", "copy", "nccl")
-        assert same == {"fused": True, "copy": True, "nccl": True, "reduce_scatter": True}
+        assert same == {"fused": True, "copy": True, "nccl": True, "reduce_scatter": True,
+                        "host_fused": True, "host_copy": True, "host_nccl": True}
