@@ -1,4 +1,5 @@
-"""Build libsrs_b200.so (the sm_100a kernels and their C ABI) in-tree.
+"""Build libsrs_b200.so (the sm_100a kernels and their C ABI) in-tree, and the
+host helper module _srs_host (C++, CPython API and libtorch headers).
 
     python stochastic-rounding-pytorch_b200/build_native.py [--force] [--verbose]
 
@@ -26,6 +27,9 @@ BUILD = HERE / "_build"
 LIBRARY = HERE / "sr_states" / "_native" / "libsrs_b200.so"
 # Test-only kernels that check device building blocks (loaded by tests/ only).
 SELFTEST = HERE / "sr_states" / "_native" / "libsrs_selftest.so"
+# Host helper of the optimizer steps (tensor signatures for the repeated-step check).
+HOST = HERE / "sr_states" / "_native" / "_srs_host.so"
+HOST_SOURCE = CSRC / "host_signature.cpp"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = [
@@ -59,10 +63,43 @@ def _sources() -> list[Path]:
 
 
 def up_to_date() -> bool:
+    return _kernels_up_to_date() and _host_up_to_date()
+
+
+def _kernels_up_to_date() -> bool:
     if not LIBRARY.exists() or not SELFTEST.exists():
         return False
     built = LIBRARY.stat().st_mtime
     return all(src.stat().st_mtime <= built for src in _sources() + [Path(__file__)])
+
+
+def _host_up_to_date() -> bool:
+    return HOST.exists() and HOST.stat().st_mtime >= max(HOST_SOURCE.stat().st_mtime,
+                                                         Path(__file__).stat().st_mtime)
+
+
+def build_host(force: bool = False) -> Path:
+    """g++ the _srs_host CPython module against the installed torch (its headers
+    for at::Tensor access, its libraries at run time)."""
+    if not force and _host_up_to_date():
+        return HOST
+    import sysconfig
+
+    import torch
+
+    torch_dir = Path(torch.__file__).resolve().parent
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = HOST.with_suffix(".so.tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           f"-I{sysconfig.get_paths()['include']}", f"-I{torch_dir / 'include'}",
+           f"-I{torch_dir / 'include' / 'torch' / 'csrc' / 'api' / 'include'}",
+           str(HOST_SOURCE), f"-L{torch_dir / 'lib'}", "-ltorch_python", "-ltorch",
+           "-ltorch_cpu", "-lc10", f"-Wl,-rpath,{torch_dir / 'lib'}", "-o", str(tmp)]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(f"g++ failed for {HOST_SOURCE.name}:\n{result.stderr}")
+    os.replace(tmp, HOST)
+    return HOST
 
 
 def _compile(unit, verbose: bool) -> str:
@@ -82,6 +119,15 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     if not force and not verbose and up_to_date():
         return LIBRARY
     BUILD.mkdir(parents=True, exist_ok=True)
+    with ThreadPoolExecutor(1) as host_pool:
+        host = host_pool.submit(build_host, force)
+        if force or verbose or not _kernels_up_to_date():
+            _build_kernels(verbose, jobs)
+        host.result()
+    return LIBRARY
+
+
+def _build_kernels(verbose: bool, jobs: int | None) -> None:
     LIBRARY.parent.mkdir(parents=True, exist_ok=True)
     jobs = jobs or min(len(UNITS), os.cpu_count() or 4)
     with ThreadPoolExecutor(jobs) as pool:
@@ -97,7 +143,6 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
         raise RuntimeError(f"link failed:\n{result.stderr}")
     os.replace(tmp, LIBRARY)
     _link_selftest(verbose)
-    return LIBRARY
 
 
 def _link_selftest(verbose: bool) -> None:

@@ -81,7 +81,8 @@ def _fast_step(optimizer, group, formats, uses_step):
     cache = group_cache(optimizer, group)
     key = fingerprint(optimizer, group, formats)
     fast = cache.fast
-    if fast is None or fast.key != key or fast.streams != current_streams(fast.launches):
+    if (key is None or fast is None or fast.key != key
+            or fast.streams != current_streams(fast.launches)):
         return cache, key, None, None
     if not uses_step:
         return cache, key, fast.launches, None

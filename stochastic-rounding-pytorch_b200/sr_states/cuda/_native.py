@@ -15,6 +15,7 @@ from pathlib import Path
 import numpy as np
 
 LIBRARY_PATH = Path(__file__).resolve().parent.parent / "_native" / "libsrs_b200.so"
+HOST_PATH = LIBRARY_PATH.parent / "_srs_host.so"
 
 SRS_OK = 0
 SRS_ERR_INVALID_ARGUMENT = -1
@@ -147,6 +148,27 @@ def load_library() -> ctypes.CDLL:
                 raise RuntimeError("libsrs_b200.so ABI version mismatch; rebuild it")
             _library = lib
     return _library
+
+
+_host = None
+
+
+def host_module():
+    """The _srs_host helper module (raises if it has not been built)."""
+    global _host
+    if _host is None:
+        import importlib.machinery
+        import importlib.util
+
+        if not HOST_PATH.exists():
+            raise RuntimeError(f"{HOST_PATH} is missing: build it with "
+                               "`python stochastic-rounding-pytorch_b200/build_native.py`")
+        loader = importlib.machinery.ExtensionFileLoader("_srs_host", str(HOST_PATH))
+        spec = importlib.util.spec_from_file_location("_srs_host", str(HOST_PATH), loader=loader)
+        module = importlib.util.module_from_spec(spec)
+        loader.exec_module(module)
+        _host = module
+    return _host
 
 
 def _check(rc: int) -> None:

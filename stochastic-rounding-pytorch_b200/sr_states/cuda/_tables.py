@@ -144,40 +144,19 @@ class FastStep:
     steps: list  # next step of every updated parameter at the last step (AdamW)
 
 
-def fingerprint(optimizer, group, formats) -> tuple:
-    """Identity, address and size of every tensor a step of ``group`` touches.
+def fingerprint(optimizer, group, formats) -> tuple | None:
+    """Identity, storage and layout of every tensor a step of ``group`` touches.
 
-    Two equal fingerprints mean the same parameter, gradient and state objects
-    at the same addresses and sizes, so the row tables, the layout checks and
-    the overlap check of the first of the two steps still hold."""
-    try:
-        return _fingerprint(optimizer.state, optimizer._state_names, group["params"], formats)
-    except RuntimeError:  # e.g. a sparse gradient has no data pointer: take the full path
-        return None
-
-
-def _fingerprint(state, names, params, formats) -> tuple:
-    # One flat tuple per parameter; written for the interpreter's speed, as it
-    # runs on every step (about 1 us per parameter).
-    parts = [tuple(formats)]
-    append, get = parts.append, state.get
-    n0 = names[0]
-    n1 = names[1] if len(names) > 1 else None
-    for p in params:
-        g = p.grad
-        if g is None:
-            append(None)
-            continue
-        st = get(p)
-        if st is None:
-            append((id(p), p.data_ptr(), p.numel(), id(g), g.data_ptr(), g.numel()))
-            continue
-        s0 = st.get(n0)
-        s1 = st.get(n1) if n1 is not None else None
-        append((id(p), p.data_ptr(), p.numel(), id(g), g.data_ptr(), g.numel(), id(st),
-                id(s0), s0.data_ptr() if s0 is not None else 0,
-                id(s1), s1.data_ptr() if s1 is not None else 0))
-    return tuple(parts)
+    Two equal fingerprints mean the same parameter, gradient, state dict and
+    state objects, at the same addresses, sizes, dtypes, shapes and
+    contiguity, so the row tables, the layout checks and the overlap check of
+    the first of the two steps still hold.  None (a tensor without strided
+    storage, e.g. a sparse gradient) sends the step down the full path, which
+    raises the proper error.  The per-tensor work runs in the _srs_host module
+    (one call instead of a Python loop over the tensors)."""
+    sig = _native.host_module().signature(group["params"], optimizer.state,
+                                           tuple(optimizer._state_names))
+    return None if sig is None else (tuple(formats), sig)
 
 
 def current_streams(launches) -> tuple:

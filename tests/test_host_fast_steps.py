@@ -123,3 +123,46 @@ def test_sparse_gradient_after_fast_steps_raises_the_reference_error(fake_launch
     p.grad = torch.sparse_coo_tensor([[0]], [1.0], size=(4,))
     with pytest.raises(RuntimeError, match="sparse"):
         opt.step()
+
+
+@pytest.mark.parametrize("change", ["grad_transposed_in_place", "param_dtype_view",
+                                    "state_transposed_in_place", "param_reshaped"])
+@pytest.mark.parametrize("cls", [AdamWReferenceSR, SGDMReferenceSR])
+def test_in_place_layout_and_dtype_changes_are_noticed(cls, change, fake_launcher):
+    """Changes that keep every object and address (in-place transposes, a dtype
+    view of the same storage, a reshape) must still reach the full preparation:
+    both twins raise the same error or take the same step."""
+    fmt = ({"exp_avg": StateFormat(torch.bfloat16), "exp_avg_sq": StateFormat(torch.bfloat16)}
+           if cls is AdamWReferenceSR else StateFormat(torch.bfloat16))
+    twins = []
+    for _ in range(2):
+        gen = torch.Generator().manual_seed(3)
+        ps = [torch.nn.Parameter(torch.randn(4, 4, generator=gen).bfloat16()),
+              torch.nn.Parameter(torch.randn(7, generator=gen).bfloat16())]
+        for p in ps:
+            p.grad = (torch.randn(p.shape, generator=gen) * 1e-2).bfloat16()
+        opt = cls(ps, lr=0.01, state_format=fmt, seed=5, **_kwargs(cls))
+        opt.step()
+        opt.step()
+        twins.append((opt, ps))
+    outcomes = []
+    for i, (opt, ps) in enumerate(twins):
+        p = ps[0]
+        if change == "grad_transposed_in_place":
+            p.grad.t_()
+        elif change == "param_dtype_view":
+            p.data = p.data.view(torch.float16)  # same bytes, another dtype
+        elif change == "state_transposed_in_place":
+            opt.state[p][opt._state_names[0]].t_()
+        elif change == "param_reshaped":
+            p.data = p.data.view(2, 8)
+        try:
+            opt.step() if i == 0 else _full_step(opt)
+            outcomes.append(None)
+        except (ValueError, TypeError, RuntimeError) as exc:
+            outcomes.append((type(exc), str(exc)))
+    assert outcomes[0] == outcomes[1]
+    if change != "param_reshaped":
+        assert outcomes[0] is not None  # the full preparation rejects these
+    if outcomes[0] is None:
+        _same(twins[0][0], twins[0][1], twins[1][0], twins[1][1])
