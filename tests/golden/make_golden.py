@@ -1,6 +1,7 @@
 """Generate the golden vectors of tests/golden/ by running the reference itself.
 
-    python tests/golden/make_golden.py [--reference /path/to/stochastic-rounding-pytorch]
+    python tests/golden/make_golden.py --reference /path/to/stochastic-rounding-pytorch
+    (or set SR_STATES_REFERENCE to that path)
 
 Imports the reference package ``sr_states`` (KristiTopollai/stochastic-rounding-pytorch,
 pure Python on PyTorch's CPU kernels) from the given checkout and records its
@@ -26,6 +27,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -427,8 +429,11 @@ def make_optimizers(ref):
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("SR_STATES_REFERENCE"),
+                        help="checkout of the reference (default: $SR_STATES_REFERENCE)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("give --reference or set SR_STATES_REFERENCE")
     sys.path.insert(0, str(Path(args.reference).resolve()))
     import sr_states as ref
     import torch
