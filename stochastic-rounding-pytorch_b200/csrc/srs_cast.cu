@@ -8,7 +8,7 @@ cudaError_t launch_cast(const float* x, void* y, int64_t n, uint32_t base, int r
                         int vec_ok, int grid_ctas, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
   const int64_t work = (n + kTile - 1) / kTile;
-  constexpr int smem = kStages * kCastStageBytes;
+  constexpr int smem = kCastStages * kCastStageBytes;
   const int grid =
       grid_for(reinterpret_cast<const void*>(&cast_kernel<OF>), work, grid_ctas, &err, smem);
   if (err != cudaSuccess) return err;

@@ -673,6 +673,14 @@ __global__ void __launch_bounds__(kThreads)
 // memory by per-thread cp.async copies of the thread's 32 input bytes, so the
 // loads of the next tile are in flight during the hashing and rounding.
 constexpr int kCastStageBytes = kThreads * kVec * 4;  // one tile of FP32 input
+#ifndef SRS_CAST_STAGES
+// Tiles in flight per thread, the current one included.  Measured on B200 at
+// 2^30 elements: 3 or 4 stages gain at most 1% on the stochastic casts and
+// cost the nearest casts (which share the kernel's shared-memory size, hence
+// its occupancy) 10-15%.
+#define SRS_CAST_STAGES 2
+#endif
+constexpr int kCastStages = SRS_CAST_STAGES;
 
 template <int OF, int RULE>
 __device__ __forceinline__ void cast_grid_stride(const float* __restrict__ x, void* __restrict__ y,
@@ -709,15 +717,20 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t full_end = min(last, n / kTile);
     const int n_full = tile < full_end ? (int)(full_end - tile) : 0;
     const uint32_t slot = (uint32_t)__cvta_generic_to_shared(stage_mem) + threadIdx.x * kVec * 4;
-    if (n_full > 0) cp_async_chunk<kVec * 4>(slot, x + e0);
-    cp_async_commit();
-    for (int i = 0; i < n_full; ++i, e0 += kTile) {
-      if (i + 1 < n_full)
-        cp_async_chunk<kVec * 4>(slot + ((i + 1) & 1) * kCastStageBytes, x + e0 + kTile);
+#pragma unroll
+    for (int d = 0; d < kCastStages - 1; ++d) {
+      if (d < n_full) cp_async_chunk<kVec * 4>(slot + d * kCastStageBytes, x + e0 + d * kTile);
       cp_async_commit();
-      cp_async_wait_stage();
-      const uint4* s = reinterpret_cast<const uint4*>(stage_mem + (i & 1) * kCastStageBytes +
-                                                      threadIdx.x * kVec * 4);
+    }
+    for (int i = 0; i < n_full; ++i, e0 += kTile) {
+      const unsigned ahead = (unsigned)i + kCastStages - 1;
+      if (ahead < (unsigned)n_full)
+        cp_async_chunk<kVec * 4>(slot + (ahead % kCastStages) * kCastStageBytes,
+                                 x + e0 + (kCastStages - 1) * kTile);
+      cp_async_commit();
+      asm volatile("cp.async.wait_group %0;" ::"n"(kCastStages - 1) : "memory");
+      const uint4* s = reinterpret_cast<const uint4*>(
+          stage_mem + ((unsigned)i % kCastStages) * kCastStageBytes + threadIdx.x * kVec * 4);
       const uint4 a = s[0], b = s[1];
       const float v[kVec] = {__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z),
                              __uint_as_float(a.w), __uint_as_float(b.x), __uint_as_float(b.y),
