@@ -15,7 +15,7 @@ import torch
 import _scenarios
 import oracle
 from _support import (DTYPE, FMT, adamw_param_close, assert_bits_or_nan, from_bits, load_json,
-                      load_npz, tbits)
+                      load_npz, tbits, ulp_distance)
 
 pytestmark = pytest.mark.gpu
 
@@ -61,6 +61,7 @@ def test_config1_matches_reference_every_step(cuda_device):
     p = torch.nn.Parameter(from_bits(a["param_init"], torch.float32, cuda_device))
     opt = AdamWReferenceSR([p], lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                            seed=7)
+    mismatched, worst = 0, 0
     for step in range(1, 11):
         previous = tbits(p).view(np.float32).copy()
         p.grad = from_bits(a[f"grad_{step}"], torch.float32, cuda_device)
@@ -69,8 +70,17 @@ def test_config1_matches_reference_every_step(cuda_device):
         assert np.array_equal(tbits(opt.state[p]["exp_avg_sq"]), a[f"exp_avg_sq_{step}"])
         assert adamw_param_close(tbits(p), a[f"param_{step}"], previous, 1.0 - 3e-4 * 0.01,
                                  32).all()
+        distance = ulp_distance(tbits(p), a[f"param_{step}"], 32)
+        mismatched += int(np.count_nonzero(distance))
+        worst = max(worst, int(distance.max()))
         with torch.no_grad():
             p.copy_(from_bits(a[f"param_{step}"], torch.float32, cuda_device))
+    # The reference's CPU sqrt is not correctly rounded (one ulp on ~0.7% of
+    # inputs); measured: 13 of 81,920 parameter values differ, by at most 2 ulp
+    # (1 ulp of u can be 2 ulp of p' under cancellation).
+    rate = mismatched / (10 * p.numel())
+    print(f"config 1 parameters vs the reference: mismatch rate {rate:.2e}, max {worst} ulp")
+    assert rate < 2e-3 and worst <= 2
 
 
 def test_config1_full_size_state_digests(cuda_device):
