@@ -622,9 +622,13 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 8030261248 / value * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4), "
-                               "CPU port timed on a sample and scaled to 8,030,261,248 params",
-                   "parallelism": "host cores"},
+        "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4)",
+                   "params": 8030261248, "tensors": 291, "param_dtype": "bf16",
+                   "grad_dtype": "bf16", "exp_avg": "float8_e4m3fn stochastic",
+                   "exp_avg_sq": "bfloat16 stochastic", "parallelism": "host cores",
+                   "global_batch": None, "seq_len": None,
+                   "timing": "each step a bounded sample of the workload, scaled to its "
+                             "8,030,261,248 parameters (see cpu_baseline.sample)"},
         "cpu_baseline": base,
         "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0}}), flush=True)
