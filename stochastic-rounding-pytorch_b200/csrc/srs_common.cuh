@@ -292,7 +292,7 @@ __device__ __forceinline__ float2 grid_stochastic2(float2 x, uint32_t h0, uint32
       __uint_as_float(__float_as_uint(fmaxf(ax, Grid<F>::kMinNormal)) & 0x7F800000u),
       __uint_as_float(__float_as_uint(fmaxf(ay, Grid<F>::kMinNormal)) & 0x7F800000u));
   const float2 n = mul2_rn(make_float2(grid_noise(h0), grid_noise(h1)), splat2(kNoise));
-  const float2 a = make_float2(__fmaf_rz(n.x, s.x, ax), __fmaf_rz(n.y, s.y, ay));
+  const float2 a = fma2_rz(n, s, make_float2(ax, ay));
   const float2 b = fma2_rz(s, splat2(kStep), a);
   const float2 y = fma2_rn(s, splat2(-kStep), b);
   return make_float2(__uint_as_float(__float_as_uint(y.x) | (__float_as_uint(x.x) & 0x80000000u)),
