@@ -98,3 +98,45 @@ def replay(spec, device, cls=None, arrays=None):
                 p.copy_(from_bits(golden, p.dtype, device).reshape(p.shape))
     assert [g["sr_step"] for g in opt.param_groups] == spec["final_sr_step"]
     return compared, mismatched
+
+
+# --------------------------------------------------------------------------
+# The reference's own optimizer regression scenario (tests/golden/regression.*,
+# recorded from the reference's scripts/record_optimizer_golden.py setup): three
+# parameters of 17, 9 and 5 elements in two groups (lr 0.01 and 0.03), FP32 or
+# BF16-nearest states, seed 2^32-13, seven steps whose gradients are
+# sin(0.137 * index + step + i), missing when (step + i) % 4 == 0.  Not teacher
+# forced: every byte after the seventh step must equal the reference's.
+
+def regression_cases():
+    return load_json("regression.json")["cases"]
+
+
+def replay_regression(case, device):
+    """Run one regression case on ``device``; returns the list of mismatches."""
+    import sr_states
+
+    cls = getattr(sr_states, case["class"])
+    pdtype = getattr(torch, case["param_dtype"].split(".")[-1])
+    state_dtype = getattr(torch, case["state_dtype"].split(".")[-1])
+    arrays = load_npz("regression.npz")
+    params = [torch.nn.Parameter(torch.linspace(-1, 1, n).to(device, pdtype))
+              for n in (17, 9, 5)]
+    opt = cls([{"params": params[:2]}, {"params": params[2:], "lr": 0.03}], lr=0.01,
+              state_dtype=state_dtype, rounding="nearest", seed=2**32 - 13)
+    for step in range(7):
+        for i, p in enumerate(params):
+            p.grad = (None if (step + i) % 4 == 0 else
+                      torch.sin(torch.arange(p.numel()).float() * 0.137 + step + i)
+                      .to(device, pdtype))
+        opt.step()
+    bad, key = [], case["key"]
+    for i, p in enumerate(params):
+        if not np.array_equal(tbits(p), arrays[f"{key}/param{i}"]):
+            bad.append(f"param{i}")
+        for name in opt._state_names:
+            if not np.array_equal(tbits(opt.state[p][name]), arrays[f"{key}/param{i}/{name}"]):
+                bad.append(f"param{i}/{name}")
+        if str(i) in case["steps"] and opt.state[p].get("step") != case["steps"][str(i)]:
+            bad.append(f"param{i}/step")
+    return bad

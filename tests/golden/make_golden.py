@@ -18,6 +18,16 @@ outputs on seeded synthetic inputs:
                    multi-parameter, multi-group optimizer scenarios (param_index, RNG
                    step, skipped gradients, AdamW bias-correction steps, mixed formats)
 
+  regression.npz / regression.json
+                   the scenario of the reference's own optimizer regression fixture
+                   (scripts/record_optimizer_golden.py, checked by
+                   tests/test_state_formats.py:44-100): AdamW and SGDM, FP32 and BF16
+                   parameters, FP32 and BF16-nearest states, 3 parameters in 2 groups,
+                   missing gradients, seed 2^32-13, 7 steps.  Recorded by running the
+                   reference here, as that test re-derives its bytes in the current
+                   environment (its committed capture is from macOS/ARM and differs on
+                   x86 for the reference itself).
+
 Only this script touches the reference; tests read the files it wrote.  Must be
 run with the reference (not this repository's sr_states) importable.
 """
@@ -427,10 +437,57 @@ def make_optimizers(ref):
     return arrays, specs
 
 
+REGRESSION_SIZES = (17, 9, 5)
+
+
+def regression_gradient(n, step, i, dtype):
+    """Gradient of parameter i at step (None when (step + i) % 4 == 0) of the
+    reference's regression scenario."""
+    import torch
+
+    if (step + i) % 4 == 0:
+        return None
+    return torch.sin(torch.arange(n).float() * 0.137 + step + i).to(dtype)
+
+
+def make_regression(ref):
+    """The reference's optimizer regression scenario, run on the reference here."""
+    import torch
+
+    arrays, cases = {}, []
+    for cls_name in ("SGDMReferenceSR", "AdamWReferenceSR"):
+        cls = getattr(ref, cls_name)
+        for policy, state_dtype in (("fp32", torch.float32), ("bf16_rn", torch.bfloat16)):
+            for pdtype in (torch.float32, torch.bfloat16):
+                params = [torch.nn.Parameter(torch.linspace(-1, 1, n).to(pdtype))
+                          for n in REGRESSION_SIZES]
+                opt = cls([{"params": params[:2]}, {"params": params[2:], "lr": 0.03}],
+                          lr=0.01, state_dtype=state_dtype, rounding="nearest",
+                          seed=2**32 - 13)
+                for step in range(7):
+                    for i, p in enumerate(params):
+                        p.grad = regression_gradient(p.numel(), step, i, pdtype)
+                    opt.step()
+                key = f"{cls_name}/{policy}/{str(pdtype).split('.')[-1]}"
+                case = {"key": key, "class": cls_name, "state_dtype": str(state_dtype),
+                        "param_dtype": str(pdtype), "steps": {}}
+                for i, p in enumerate(params):
+                    arrays[f"{key}/param{i}"] = bits(p)
+                    for name, value in opt.state[p].items():
+                        if isinstance(value, torch.Tensor):
+                            arrays[f"{key}/param{i}/{name}"] = bits(value)
+                        else:
+                            case["steps"][str(i)] = value
+                cases.append(case)
+    return arrays, cases
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--reference", default=os.environ.get("SR_STATES_REFERENCE"),
                         help="checkout of the reference (default: $SR_STATES_REFERENCE)")
+    parser.add_argument("--only", choices=("regression",), default=None,
+                        help="write one fixture family only")
     args = parser.parse_args()
     if not args.reference:
         parser.error("give --reference or set SR_STATES_REFERENCE")
@@ -443,6 +500,11 @@ def main():
     meta = {"generator": "tests/golden/make_golden.py", "torch": str(torch.__version__),
             "reference_version": getattr(ref, "__version__", "?")}
 
+    arrays, cases = make_regression(ref)
+    np.savez_compressed(HERE / "regression.npz", **arrays)
+    (HERE / "regression.json").write_text(json.dumps({"meta": meta, "cases": cases}, indent=1))
+    if args.only == "regression":
+        return
     (HERE / "keys.json").write_text(json.dumps({"meta": meta, **make_keys(ref)}))
     arrays, manifest = make_casts(ref)
     np.savez_compressed(HERE / "casts.npz", **arrays)

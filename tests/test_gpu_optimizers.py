@@ -304,3 +304,11 @@ def test_adamw_denominator_over_every_exponent_matches_oracle(beta2, step, cuda_
     cuda_adamw_step_(*dev, seed=9, rounding="nearest", **opts)
     for got, want in zip(dev, host):
         assert_bits_or_nan(tbits(got), want.view(np.uint32), oracle.F32)
+
+
+@pytest.mark.parametrize("case", _scenarios.regression_cases(), ids=lambda c: c["key"])
+def test_regression_scenario_matches_reference(case, cuda_device):
+    """The reference's own optimizer regression scenario on the sm_100a kernels:
+    every byte after seven steps equals the reference's, AdamW FP32 parameters
+    included (the scenario's square roots are all correctly rounded on the CPU)."""
+    assert _scenarios.replay_regression(case, cuda_device) == []

@@ -6,6 +6,7 @@ import hashlib
 import numpy as np
 import pytest
 
+import _scenarios
 import oracle
 from _support import adamw_param_close, load_json, load_npz, ulp_distance
 
@@ -115,3 +116,11 @@ def test_oracle_config1_full_size_state_digests():
         _config1_step(p, g, m, v, entry["step"])
         assert hashlib.sha256(m.tobytes()).hexdigest() == entry["exp_avg_sha256"]
         assert hashlib.sha256(v.tobytes()).hexdigest() == entry["exp_avg_sq_sha256"]
+
+
+@pytest.mark.parametrize("case", _scenarios.regression_cases(), ids=lambda c: c["key"])
+def test_regression_scenario_matches_reference(case, fake_launcher):
+    """The reference's own optimizer regression scenario through the host code
+    and the oracle (CPU): every parameter, state and step byte after seven
+    steps, AdamW FP32 parameters included."""
+    assert _scenarios.replay_regression(case, "cpu") == []
