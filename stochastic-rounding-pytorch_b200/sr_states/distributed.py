@@ -345,9 +345,11 @@ class _ZeroMixin:
         peers, starts, ok = _native.SrsPeers(), {d: [] for d in buffers}, True
         try:
             n = 0
-            for r in range(self._world):
-                if r == self._rank:
-                    continue
+            # Peers in rotated order (rank+1, rank+2, ...): the kernel's peer
+            # stores and the copy streams of every rank start at a different
+            # destination, so no GPU receives everyone's first writes at once.
+            for k in range(1, self._world):
+                r = (self._rank + k) % self._world
                 for dtype, buf in buffers.items():
                     handle, offset = everyone[r][str(dtype)]
                     base = launcher.ipc_import(handle)
