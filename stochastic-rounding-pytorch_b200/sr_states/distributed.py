@@ -128,6 +128,13 @@ class FlatLayout:
         return (lo, hi) if lo < hi else None
 
 
+def peer_order(rank: int, world: int) -> list[int]:
+    """The other ranks in rotated order (rank+1, rank+2, ... mod world): the
+    kernel's peer stores and the copy streams of every rank then start at a
+    different destination, so no GPU receives everyone's first writes at once."""
+    return [(rank + k) % world for k in range(1, world)]
+
+
 class _HostIO:
     """The pinned host buffers of one ``step_host`` call."""
 
@@ -345,11 +352,7 @@ class _ZeroMixin:
         peers, starts, ok = _native.SrsPeers(), {d: [] for d in buffers}, True
         try:
             n = 0
-            # Peers in rotated order (rank+1, rank+2, ...): the kernel's peer
-            # stores and the copy streams of every rank start at a different
-            # destination, so no GPU receives everyone's first writes at once.
-            for k in range(1, self._world):
-                r = (self._rank + k) % self._world
+            for r in peer_order(self._rank, self._world):
                 for dtype, buf in buffers.items():
                     handle, offset = everyone[r][str(dtype)]
                     base = launcher.ipc_import(handle)

@@ -248,3 +248,15 @@ def test_zero_reduce_scattered_gradients_equal_unsharded_mean_gradients(world):
         if p.is_alive():
             p.kill()
     assert results == {r: "ok" for r in range(world)}, results
+
+
+def test_peer_order_rotates_destinations():
+    from sr_states.distributed import peer_order
+
+    for world in (2, 3, 4, 8):
+        orders = [peer_order(r, world) for r in range(world)]
+        for r, order in enumerate(orders):
+            assert sorted(order) == [q for q in range(world) if q != r]
+        # At every position each rank is the destination of exactly one rank.
+        for k in range(world - 1):
+            assert sorted(order[k] for order in orders) == list(range(world))
