@@ -43,7 +43,6 @@ parameters required).
 
 from __future__ import annotations
 
-import math
 
 import torch
 
@@ -82,8 +81,7 @@ class FlatLayout:
         for dtype, plist in by_dtype.items():
             total = sum(p.numel() for p in plist)
             self.numel[dtype] = total
-            unit = world * SHARD_ALIGN
-            padded = -(-total // unit) * unit
+            padded = shard_sizes(total, world) * world
             buffer = self._adopt(plist, padded)
             if buffer is None:
                 buffer = torch.zeros(padded, dtype=dtype, device=plist[0].device)
@@ -697,6 +695,7 @@ class ZeroSGDM(_ZeroMixin, SGDMReferenceSR):
 
 
 def shard_sizes(numel_total: int, world: int) -> int:
-    """Elements per shard of a flat buffer of ``numel_total`` elements."""
+    """Elements per shard of a flat buffer of ``numel_total`` elements (the
+    buffer is padded to a multiple of ``world * SHARD_ALIGN``)."""
     unit = world * SHARD_ALIGN
-    return math.ceil(numel_total / unit) * unit // world
+    return -(-numel_total // unit) * unit // world
