@@ -142,7 +142,7 @@ int srs_cast(const float* x, void* y, int64_t n, int out_format, int rule, uint3
 
 /* ---- fused multi-tensor steps -------------------------------------------
  * Replace the per-bucket launches of sr_states/triton/adamw.py:303-317
- * (_multi_adamw_kernel) and sr_states/triton/sgd.py:542-556
+ * (_multi_adamw_kernel) and sr_states/triton/sgd.py:214-237
  * (_multi_sgdm_kernel): ONE launch covers every row of a parameter group on
  * one device, whatever the rows' parameter/gradient dtypes and AdamW
  * bias-correction steps.  `rows` is a device array of n_rows srs_row;

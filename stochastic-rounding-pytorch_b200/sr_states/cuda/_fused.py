@@ -2,7 +2,7 @@
 
 These implement the ``_step_group`` plugin hook (reference:
 sr_states/optim/_state.py:172-182, overridden by sr_states/triton/adamw.py:289-319
-and sr_states/triton/sgd.py:533-556).  Every error surfaces before the first
+and sr_states/triton/sgd.py:214-237).  Every error surfaces before the first
 launch; after the launches each AdamW state records its new step.
 """
 

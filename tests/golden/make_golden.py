@@ -217,7 +217,7 @@ def make_casts(ref):
 
 def make_functional(ref):
     """adamw_step_/sgdm_step_ on 1031 elements at offset 2^32-211 with dyadic gradients
-    (tests/test_triton_states.py:286-316)."""
+    (tests/test_triton_states.py:37-64)."""
     import torch
     from sr_states._hash import update_key
     from sr_states.reference.adamw import adamw_step_

@@ -60,7 +60,7 @@ def test_empirical_up_probability_and_mean(fmt, ulp, cuda_device):
 @pytest.mark.parametrize("fmt,lo,hi", [(oracle.BF16, -20, 21), (oracle.F16, -12, 15),
                                        (oracle.E4M3, -4, 8), (oracle.E5M2, -12, 15)])
 def test_distribution_stress_is_unbiased_in_aggregate(fmt, lo, hi, cuda_device):
-    """tests/test_sr_statistics.py:29-37, over each format's normal range."""
+    """tests/test_sr_statistics.py:28-36, over each format's normal range."""
     base = torch.pow(2.0, torch.arange(lo, hi, dtype=torch.float32))
     inputs = (base[:, None] * (1.0 + torch.linspace(0.01, 0.99, 1024)[None, :])).flatten()
     reps = 64 if fmt in (oracle.E4M3, oracle.E5M2) else 1  # coarse grids: more samples
