@@ -221,12 +221,17 @@ int srs_ipc_close(void* base);
  * allocator is reserved or already full, or a step issued from code that must
  * not call into any allocator).  `host_rows` is a HOST array of n_rows srs_row,
  * copied on `stream` into a fixed device-resident table of
- * SRS_NOALLOC_MAX_ROWS rows that every call on a device shares.  Pageable
- * host_rows may be reused once the call returns; page-locked host_rows must
- * stay unchanged until the step has run on the stream.  The parameter/gradient
+ * SRS_NOALLOC_MAX_ROWS rows that every call on a device shares.  The copy is an
+ * ordinary host-to-device cudaMemcpyAsync on `stream`: keep host_rows valid and
+ * unchanged until the step has run on the stream.  The parameter/gradient
  * dtype kind is read from the rows.
  * Limits and rules:
  *   - n_rows > SRS_NOALLOC_MAX_ROWS fails with SRS_ERR_INVALID_ARGUMENT;
+ *   - rows are checked on the host before anything is enqueued: tile_begin
+ *     prefix sums, n_tiles, step classes, null addresses, and the alignment a
+ *     row's SRS_ROW_VECTOR_OK flag promises (16 bytes for parameters,
+ *     gradients and 2- or 4-byte states, 8 bytes for FP8 states); a violation
+ *     fails with SRS_ERR_INVALID_ARGUMENT;
  *   - the first call on a device looks up the table's address (set-up); make
  *     that first call before any stream capture;
  *   - calls on one device that can overlap in time (different streams or host

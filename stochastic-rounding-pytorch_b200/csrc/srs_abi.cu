@@ -578,10 +578,18 @@ int noalloc_table(srs_row** table) {
   return SRS_OK;
 }
 
+// Alignment SRS_ROW_VECTOR_OK promises for an array of `elem_bytes`-byte
+// elements: the 8-element vector accesses and cp.async copies of the kernels
+// move 16 bytes at a time (8 for one-byte FP8 states).
+uint64_t vector_alignment(int elem_bytes) { return elem_bytes == 1 ? 8u : 16u; }
+
 // Host-side check of a row table: tile_begin prefix sums, n_tiles, step
-// classes and addresses.  Returns the dtype kind the rows share (or mixed).
+// classes, addresses, and that every row flagged SRS_ROW_VECTOR_OK has the
+// alignment the flag promises (a wrongly flagged row would send the kernel
+// into misaligned vector accesses).  Returns the dtype kind the rows share
+// (or mixed).
 int check_host_rows(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int n_classes,
-                    uint32_t* kind) {
+                    int m_format, int v_format, uint32_t* kind) {
   int64_t tile = 0;
   uint32_t first = rows[0].flags & 3u;
   *kind = first;
@@ -598,6 +606,18 @@ int check_host_rows(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int n_
     if (row.numel > 0 && (row.param == 0 || row.grad == 0 || row.state[0] == 0 ||
                           row.state[1] == 0))
       return fail(SRS_ERR_INVALID_ARGUMENT, "row %lld: null address", (long long)r);
+    if ((row.flags & SRS_ROW_VECTOR_OK) != 0u) {
+      const uint64_t need_p = vector_alignment((row.flags & SRS_ROW_PARAM_BF16) ? 2 : 4);
+      const uint64_t need_g = vector_alignment((row.flags & SRS_ROW_GRAD_BF16) ? 2 : 4);
+      const uint64_t need_m = vector_alignment(fmt_bytes(m_format));
+      const uint64_t need_v = vector_alignment(fmt_bytes(v_format));
+      if (row.param % need_p != 0u || row.grad % need_g != 0u || row.state[0] % need_m != 0u ||
+          row.state[1] % need_v != 0u)
+        return fail(SRS_ERR_INVALID_ARGUMENT,
+                    "row %lld: SRS_ROW_VECTOR_OK set but an address is not aligned for vector "
+                    "access (param and grad need 16 bytes, states 16 bytes, 8 for FP8)",
+                    (long long)r);
+    }
     if ((row.flags & 3u) != first) *kind = SRS_KIND_MIXED;
     tile += (row.numel + kTile - 1) / kTile;
   }
@@ -636,15 +656,17 @@ extern "C" int srs_adamw_multi_noalloc(const srs_row* host_rows, int64_t n_rows,
   }
   if (host_rows == nullptr) return fail(SRS_ERR_INVALID_ARGUMENT, "null row table");
   uint32_t kind = 0;
-  if (int rc = check_host_rows(host_rows, n_rows, n_tiles, hp->n_step_classes, &kind)) return rc;
+  if (int rc = check_host_rows(host_rows, n_rows, n_tiles, hp->n_step_classes, m_format,
+                               v_format, &kind))
+    return rc;
   if (n_tiles == 0) return SRS_OK;
   if (int rc = check_device()) return rc;
   srs_row* table = nullptr;
   if (int rc = noalloc_table(&table)) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Stream-ordered: the kernel below (and any later call's copy on this stream)
-  // sees exactly these rows.  From pageable memory the copy has consumed
-  // host_rows when it returns; from page-locked memory it reads them later.
+  // sees exactly these rows.  The copy may read host_rows at any time until it
+  // has run on the stream, so the caller keeps them valid until then.
   cudaError_t e = cudaMemcpyAsync(table, host_rows, (size_t)n_rows * sizeof(srs_row),
                                   cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return cuda_fail(e, "srs_adamw_multi_noalloc row copy");

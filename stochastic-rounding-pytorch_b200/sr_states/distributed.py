@@ -43,6 +43,7 @@ parameters required).
 
 from __future__ import annotations
 
+import collections
 
 import torch
 
@@ -99,8 +100,11 @@ class FlatLayout:
 
     @staticmethod
     def _adopt(plist, padded):
-        """The existing storage, if the parameters already sit back to back from
-        its start and it is long enough for the padded layout."""
+        """The existing storage, if the parameters fill it exactly, back to back
+        from its start, and the layout needs no padding.  Anything else in the
+        storage (a frozen tensor stored after the parameters, say) would be
+        overwritten by the padding's all-gather, so such storage is never
+        adopted and the parameters move into a fresh buffer instead."""
         storage = plist[0].untyped_storage()
         offset = 0
         for p in plist:
@@ -108,7 +112,7 @@ class FlatLayout:
                     or p.storage_offset() != offset):
                 return None
             offset += p.numel()
-        if storage.nbytes() < padded * plist[0].element_size():
+        if offset != padded or storage.nbytes() != padded * plist[0].element_size():
             return None
         base = torch.empty(0, dtype=plist[0].dtype, device=plist[0].device).set_(
             storage, 0, (padded,), (1,))
@@ -268,7 +272,7 @@ class _ZeroMixin:
     """ZeRO-1 behaviour for a fused StateOptimizer subclass (see module docstring)."""
 
     def __init__(self, params, *args, process_group=None, gather="auto", chunks=32,
-                 grads="full", **kwargs):
+                 grads="full", record_timings=False, **kwargs):
         if gather not in ("auto", "fused", "copy", "nccl"):
             raise ValueError(f"gather must be 'auto', 'fused', 'copy' or 'nccl', got {gather!r}")
         if grads not in ("full", "reduce_scatter"):
@@ -280,7 +284,10 @@ class _ZeroMixin:
         self._rank = torch.distributed.get_rank(process_group) if initialized else 0
         ordered = [p for g in self.param_groups for p in g["params"]]
         self._layout = FlatLayout(ordered, self._world, self._rank)
-        self._events: list = []
+        # CUDA events of the last steps (record_timings=True); bounded, so a run
+        # that never reads `timings` keeps at most this many steps' events.
+        self._record_timings = bool(record_timings)
+        self._events: collections.deque = collections.deque(maxlen=4096)
         self._timed: list = []
         self._grad_buffers: dict[torch.dtype, torch.Tensor] = {}
         if grads == "reduce_scatter":
@@ -315,12 +322,30 @@ class _ZeroMixin:
             self._gather = "fused"
         else:
             self._gather = "copy" if self._srs_exchange is not None else "nccl"
+        self._connected_gather = self._gather
+        self._connected = (self._srs_peers, self._srs_exchange)
 
     @property
     def gather_mode(self) -> str:
         """'fused' (peer stores inside the step), 'copy' (copy engines pipelined
         with the step), 'nccl' (all-gather after it) or 'none' (one rank)."""
         return self._gather
+
+    def set_gather_mode(self, mode: str) -> None:
+        """Switch between the exchange chosen at construction and the NCCL
+        all-gather, for the following steps (every rank must switch together).
+        Both deliver the same parameters; the NCCL form runs the update as a
+        launch of its own, which is how the update alone is timed."""
+        if self._world == 1:
+            if mode != "none":
+                raise ValueError("a single rank has no exchange (gather mode 'none')")
+            return
+        if mode not in ("nccl", self._connected_gather):
+            raise ValueError(f"gather mode must be 'nccl' or {self._connected_gather!r}, "
+                             f"got {mode!r}")
+        self._gather = mode
+        self._srs_peers, self._srs_exchange = (
+            self._connected if mode == self._connected_gather else (None, None))
 
     def _agree(self, value):
         """Every rank's ``value`` (a collective: all ranks call it together)."""
@@ -553,7 +578,8 @@ class _ZeroMixin:
 
     @torch.no_grad()
     def step(self, closure=None):
-        stream = torch.cuda.current_stream() if torch.cuda.is_available() else None
+        stream = (torch.cuda.current_stream()
+                  if self._record_timings and torch.cuda.is_available() else None)
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if stream else None
         fused = self._gather in ("fused", "copy")
         if marks:
@@ -618,11 +644,16 @@ class _ZeroMixin:
         pipeline = self._srs_exchange
         restore = pipeline
         if pipeline is None:
+            # One full launch when the kernel itself stores to the peers; tile
+            # ranges otherwise.  One cached pipeline per kind.
+            whole = self._srs_peers is not None
             if self._host_pipeline is None:
+                self._host_pipeline = {}
+            if whole not in self._host_pipeline:
                 device = next(iter(self._layout.buffers.values())).device
-                self._host_pipeline = _ChunkedExchange(self._layout, None, device, self._chunks,
-                                                       whole=self._srs_peers is not None)
-            pipeline = self._srs_exchange = self._host_pipeline
+                self._host_pipeline[whole] = _ChunkedExchange(self._layout, None, device,
+                                                              self._chunks, whole=whole)
+            pipeline = self._srs_exchange = self._host_pipeline[whole]
         pipeline.host = _HostIO(grads, params, self._grad_buffers)
         try:
             return self.step()
@@ -650,22 +681,23 @@ class _ZeroMixin:
 
     @property
     def timings(self):
-        """Per step since the last clear: update_ms (the fused launches, including
-        their peer stores when the gather is fused) and gather_ms (the barriers
-        around a fused step, or the NCCL all-gather); reading it synchronizes on
-        the recorded events."""
+        """Per step since the last clear (only with ``record_timings=True``):
+        update_ms (the fused launches, including their peer stores when the
+        gather is fused) and gather_ms (the barriers around a fused step, or the
+        NCCL all-gather); reading it synchronizes on the recorded events."""
         for marks in self._events:
             marks[3].synchronize()
             self._timed.append({"update_ms": marks[1].elapsed_time(marks[2]),
                                 "gather_ms": marks[0].elapsed_time(marks[1])
                                 + marks[2].elapsed_time(marks[3])})
-        self._events = []
+        self._events.clear()
         return _TimingList(self._timed)
 
     def close(self):
         """Drop recorded timings and unmap the peers' buffers (call after the last
         step, on every rank, while the process group still exists)."""
-        self._events, self._timed = [], []
+        self._events.clear()
+        self._timed = []
         if self._srs_exchange is not None:
             torch.cuda.current_stream().synchronize()
         self._close_peers()
@@ -674,6 +706,8 @@ class _ZeroMixin:
         self._host_pipeline = None
         if self._gather in ("fused", "copy"):
             self._gather = "nccl"  # a later step all-gathers
+        self._connected_gather = self._gather if self._world > 1 else "none"
+        self._connected = (None, None)
 
 
 class _TimingList(list):

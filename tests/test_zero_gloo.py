@@ -260,3 +260,77 @@ def test_peer_order_rotates_destinations():
         # At every position each rank is the destination of exactly one rank.
         for k in range(world - 1):
             assert sorted(order[k] for order in orders) == list(range(world))
+
+
+def _spawn(worker, world):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+def _shared_storage_worker(rank, world, port, queue):
+    sys.path[:0] = [str(ROOT), str(ROOT / "stochastic-rounding-pytorch_b200"), str(ROOT / "tests")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    from _support import FakeLauncher
+    from sr_states import AdamWReferenceSR
+    from sr_states.cuda import _native
+    from sr_states.distributed import ZeroAdamW
+
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        _native.set_launcher(FakeLauncher())
+        # Two parameters back to back, then a frozen tensor in the same storage,
+        # different on every rank (as rank-local data would be).
+        storage = torch.randn(1000 + 200, generator=torch.Generator().manual_seed(5))
+        storage[1000:] = float(rank + 1)
+        params = [torch.nn.Parameter(storage[:600].view(20, 30)),
+                  torch.nn.Parameter(storage[600:1000])]
+        frozen = storage[1000:]
+        before = frozen.clone()
+        reference = [torch.nn.Parameter(p.detach().clone()) for p in params]
+        opt = ZeroAdamW(params, lr=1e-2, seed=3)
+        ref_opt = AdamWReferenceSR(reference, lr=1e-2, seed=3)
+        assert opt.gather_mode == "nccl"
+        opt.set_gather_mode("nccl")
+        try:
+            opt.set_gather_mode("fused")
+            raise AssertionError("a mode that was never connected must be refused")
+        except ValueError:
+            pass
+        for step in range(2):
+            for p, q in zip(params, reference):
+                g = torch.randn(p.shape, generator=torch.Generator().manual_seed(step))
+                p.grad, q.grad = g.clone(), g.clone()
+            opt.step()
+            ref_opt.step()
+        assert torch.equal(frozen, before), "the frozen tensor after the parameters changed"
+        for p, q in zip(params, reference):
+            assert torch.equal(p.detach(), q.detach())
+        queue.put((rank, "ok"))
+    except BaseException:  # report, never hang the parent
+        import traceback
+        queue.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_zero_never_adopts_storage_shared_with_other_tensors():
+    """Parameters that share their storage with a tensor stored after them move to
+    a fresh flat buffer, so the padding's all-gather cannot overwrite that tensor."""
+    results = _spawn(_shared_storage_worker, 2)
+    assert results == {0: "ok", 1: "ok"}, results

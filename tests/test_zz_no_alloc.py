@@ -1,11 +1,17 @@
 """srs_adamw_multi_noalloc, the multi-tensor AdamW step that allocates no device
 memory (its row table lives in a fixed table of the library's device image),
-against srs_adamw_multi, whose row table the caller allocates.
+against srs_adamw_multi, whose row table the caller allocates, and against the
+CPU oracle.
 
-Both entry points launch the same kernel on the same rows, so two steps in a
-row must leave bit-identical parameters and states (tolerance: exact).  This
-file is named to be collected last, so the GPU test runs both alone in a fresh
-process and after every other test has used the library.
+Some callers cannot allocate device memory while they step: a runtime that
+hands all of HBM to its own arena up front, or code that must not enter an
+allocator at step time.  This entry point serves them.  Both entry points
+launch the same kernel on the same rows, so two steps in a row must leave
+bit-identical parameters and states (tolerance: exact), and the oracle, which
+follows the same operation order with a correctly rounded square root, must
+agree byte for byte too.  This file is named to be collected last, so the GPU
+test runs both alone in a fresh process and after every other test has used
+the library.
 """
 
 import ctypes
@@ -14,6 +20,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from sr_states.cuda import _native
 
 SEED = 1234
@@ -82,6 +89,30 @@ def check(lib, rc):
     assert rc == _native.SRS_OK, lib.srs_last_error().decode()
 
 
+def host_copy(row):
+    """CPU numpy copies of a row's (param, grad, m, v) in the oracle's bit layouts."""
+    out = []
+    for t in row:
+        if t.dtype == torch.float32:
+            out.append(t.cpu().numpy().copy())
+        else:
+            size = t.element_size()
+            raw = t.view(torch.int16 if size == 2 else torch.uint8).cpu().numpy()
+            out.append(raw.view(np.uint16 if size == 2 else np.uint8).copy())
+    return out
+
+
+def oracle_step(spec, cpu_rows, hp, step):
+    """The same multi-tensor step on the CPU oracle, row by row."""
+    for index, ((numel, p_dtype, g_dtype, cls), (p, g, m, v)) in enumerate(zip(spec, cpu_rows)):
+        scalars = [hp.beta1, hp.beta2, hp.one_minus_beta1, hp.one_minus_beta2, hp.eps, hp.decay,
+                   hp.neg_step_size[cls], hp.bias2_sqrt[cls]]
+        oracle.adamw_core_at(p.ctypes.data, int(p_dtype == torch.bfloat16), g.ctypes.data,
+                             int(g_dtype == torch.bfloat16), m.ctypes.data, oracle.E4M3,
+                             oracle.STOCHASTIC, v.ctypes.data, oracle.BF16, oracle.STOCHASTIC,
+                             numel, scalars, oracle.update_key(SEED, step, index), 0)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("spec", [ROWS, UNIFORM], ids=["mixed-dtypes", "bf16"])
 def test_noalloc_matches_allocating_entry_point_two_steps_in_a_row(cuda_device, spec):
@@ -95,25 +126,36 @@ def test_noalloc_matches_allocating_entry_point_two_steps_in_a_row(cuda_device, 
     device_table = torch.from_numpy(table_theirs.view(np.uint8)).to(cuda_device)
     stream = torch.cuda.current_stream(cuda_device).cuda_stream
 
+    expected = [host_copy(row) for row in ours]
+
     for call, steps in enumerate([(1, 2), (2, 3)]):
         hp, words = hparams(steps), rng(call + 1)
         check(lib, lib.srs_adamw_multi(device_table.data_ptr(), len(spec), n_tiles, E4M3, SR,
                                        BF16, SR, ctypes.byref(hp), ctypes.byref(words),
                                        uniform_kind(table_theirs), 0, stream))
+        torch.cuda.synchronize(cuda_device)
         allocated = torch.cuda.memory_stats(cuda_device).get("allocation.all.allocated", 0)
+        free_before = torch.cuda.mem_get_info(cuda_device)[0]
         check(lib, lib.srs_adamw_multi_noalloc(table_ours.ctypes.data, len(spec), n_tiles, E4M3,
                                                SR, BF16, SR, ctypes.byref(hp),
                                                ctypes.byref(words), 0, stream))
-        assert torch.cuda.memory_stats(cuda_device).get("allocation.all.allocated", 0) == allocated
         torch.cuda.synchronize(cuda_device)
-        for r, (a_row, b_row) in enumerate(zip(ours, theirs)):
-            for name, a, b in zip(("param", "grad", "m", "v"), a_row, b_row):
+        assert torch.cuda.memory_stats(cuda_device).get("allocation.all.allocated", 0) == allocated
+        if call > 0:  # the first call may load the module that holds the table
+            assert torch.cuda.mem_get_info(cuda_device)[0] == free_before
+        oracle_step(spec, expected, hp, call + 1)
+        for r, (a_row, b_row, e_row) in enumerate(zip(ours, theirs, expected)):
+            for name, a, b, e in zip(("param", "grad", "m", "v"), a_row, b_row, e_row):
                 assert np.array_equal(bits(a), bits(b)), f"call {call}: row {r} {name} differs"
+                assert np.array_equal(bits(a), e.view(np.uint8)), (
+                    f"call {call}: row {r} {name} differs from the oracle")
         assert any(bool(row[2].float().abs().sum() > 0) for row in ours)  # the step ran
         # Fresh gradients, identical for both sets, before the next call.
         for a_row, b_row in zip(ours, theirs):
             a_row[1].copy_(torch.randn(a_row[1].numel(), generator=generator).to(a_row[1]))
             b_row[1].copy_(a_row[1])
+        for a_row, e_row in zip(ours, expected):
+            e_row[1] = host_copy(a_row)[1]
 
 
 def test_noalloc_rejects_oversized_and_inconsistent_tables_before_any_device_call():
@@ -142,3 +184,41 @@ def test_noalloc_rejects_oversized_and_inconsistent_tables_before_any_device_cal
     assert rc == _native.SRS_ERR_INVALID_ARGUMENT and b"step class" in lib.srs_last_error()
     assert lib.srs_adamw_multi_noalloc(None, 0, 0, 3, 1, 1, 1, ctypes.byref(hp),
                                        ctypes.byref(words), 0, None) == _native.SRS_OK
+
+
+def test_noalloc_rejects_a_vector_flag_on_misaligned_rows():
+    """A row flagged SRS_ROW_VECTOR_OK whose addresses lack the promised alignment
+    is refused on the host.  Every table here also carries a wrong n_tiles (the
+    row holds 2 tiles, 3 are claimed), which the host check reports after the
+    rows, so no call can reach the GPU even if a row check were missing."""
+    lib = _native.load_library()
+    hp, words = hparams((1,)), rng(1)
+    table = np.zeros(1, dtype=_native.ROW_DTYPE)
+    table["numel"] = 4096
+    table["param"], table["grad"] = 0x10000, 0x20000
+    table["state"] = (0x30000, 0x40000)
+    table["flags"] = _native.ROW_VECTOR_OK | _native.ROW_PARAM_BF16 | _native.ROW_GRAD_BF16
+
+    def message(rows):
+        rc = lib.srs_adamw_multi_noalloc(rows.ctypes.data, 1, 3, E4M3, SR, BF16, SR,
+                                         ctypes.byref(hp), ctypes.byref(words), 0, None)
+        assert rc == _native.SRS_ERR_INVALID_ARGUMENT
+        return lib.srs_last_error()
+
+    for field, index, address in (("param", None, 0x10002), ("grad", None, 0x20008),
+                                  ("state", 0, 0x30004), ("state", 1, 0x40008)):
+        bad = table.copy()
+        if index is None:
+            bad[field] = address
+        else:
+            bad[field][0, index] = address
+        assert b"SRS_ROW_VECTOR_OK" in message(bad), (field, index)
+    # An FP8 state needs only 8 bytes, and without the flag any alignment passes
+    # the row check: these tables fail on n_tiles only.
+    fp8_ok = table.copy()
+    fp8_ok["state"][0, 0] = 0x30008
+    unflagged = table.copy()
+    unflagged["param"] = 0x10002
+    unflagged["flags"] = _native.ROW_PARAM_BF16 | _native.ROW_GRAD_BF16
+    for good in (table, fp8_ok, unflagged):
+        assert b"n_tiles" in message(good)
