@@ -56,6 +56,11 @@ BYTES_PER_PARAM = 12
 # many bytes per parameter.
 MEASURED_TRAFFIC_PER_PARAM = 11.913
 FALLBACK_HBM_GBS = 6650.0
+# BASELINE config 4 hyperparameters.
+LR, BETAS, EPS, WEIGHT_DECAY, SEED = 3e-4, (0.9, 0.999), 1e-8, 0.1, 7
+# Measured peer copy bandwidth per direction and GPU over NVLink 5 on this pool
+# (copy engines); nominal 900 GB/s.
+NVLINK_PEER_GBS = 770.0
 
 
 def parse_args(argv=None):
@@ -193,9 +198,10 @@ def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunk
     from sr_states.distributed import ZeroAdamW
     from sr_states.shapes import llama3_8b
 
-    shapes = [s for name, s in llama3_8b()
-              if (embeddings or name not in ("embed_tokens", "lm_head"))
-              and not (name.startswith("layers.") and int(name.split(".")[1]) >= layers)]
+    named = [(name, s) for name, s in llama3_8b()
+             if (embeddings or name not in ("embed_tokens", "lm_head"))
+             and not (name.startswith("layers.") and int(name.split(".")[1]) >= layers)]
+    names, shapes = [n for n, _ in named], [s for _, s in named]
     total = sum(math.prod(s) for s in shapes)
     device = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=device).manual_seed(7)
@@ -210,12 +216,12 @@ def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunk
            "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
     # Flat gradient buffers (every p.grad a view into them): the layout the
     # host-streamed step of the e2e measurement loads into.
-    opt = ZeroAdamW(params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1,
-                    state_format=fmt, seed=7, gather=gather, chunks=chunks,
-                    grads="reduce_scatter")
+    opt = ZeroAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WEIGHT_DECAY,
+                    state_format=fmt, seed=SEED, gather=gather, chunks=chunks,
+                    grads="reduce_scatter", record_timings=True)
     flat_g = opt.flat_grads(torch.bfloat16)
     flat_g.normal_(0, 1e-4, generator=gen)
-    return opt, params, flat_p, flat_g, total
+    return opt, names, params, flat_p, flat_g, total
 
 
 def time_steps(opt, steps, world, stream):
@@ -250,7 +256,7 @@ def cpu_baseline(seconds):
     import oracle
 
     threads = oracle.cpu_threads()
-    n = 1 << 22
+    n = 1 << 24
     rng = np.random.default_rng(7)
     p = (rng.standard_normal(n, dtype=np.float32) * 0.02).view(np.uint32) >> 16
     g = (rng.standard_normal(n, dtype=np.float32) * 1e-4).view(np.uint32) >> 16
@@ -260,22 +266,264 @@ def cpu_baseline(seconds):
 
     def one_pass(step):
         oracle.adamw_(p, g, m, v, m_fmt=oracle.E4M3, m_rule=oracle.STOCHASTIC,
-                      v_fmt=oracle.BF16, v_rule=oracle.STOCHASTIC, lr=3e-4, beta1=0.9,
-                      beta2=0.999, eps=1e-8, weight_decay=0.1, step=step,
-                      update_key=oracle.update_key(7, step, 0), threads=threads)
+                      v_fmt=oracle.BF16, v_rule=oracle.STOCHASTIC, lr=LR, beta1=BETAS[0],
+                      beta2=BETAS[1], eps=EPS, weight_decay=WEIGHT_DECAY, step=step,
+                      update_key=oracle.update_key(SEED, step, 0), threads=threads)
 
     one_pass(1)  # warm-up (page faults)
-    passes, start = 0, time.perf_counter()
+    rates = []
+    start = time.perf_counter()
     while True:
-        one_pass(passes + 2)
-        passes += 1
+        t = time.perf_counter()
+        one_pass(len(rates) + 2)
+        rates.append(n / (time.perf_counter() - t))
         elapsed = time.perf_counter() - start
-        if elapsed * threads >= seconds or elapsed >= seconds:
+        if elapsed >= seconds:
             break
-    rate = passes * n / elapsed
-    return {"value": rate, "unit": "params/s", "cores": threads, "kind": "port",
-            "sample": f"{passes} passes over {n} elements (BF16 p/g, E4M3 SR m, BF16 SR v), "
-                      f"{elapsed:.2f} s wall on {threads} threads"}
+    return {"value": statistics.median(rates), "unit": "params/s", "cores": threads,
+            "kind": "port",
+            "sample": f"median of {len(rates)} passes over {n} elements (BF16 p/g, E4M3 SR m, "
+                      f"BF16 SR v) of the C restatement, {elapsed:.2f} s wall on {threads} "
+                      "threads"}
+
+
+REFERENCE_DIR = ROOT / "baseline" / "_ref"
+REFERENCE_SAMPLE = 1 << 24  # elements of the reference arm's sample tensor
+
+
+def reference_cpu_steps(steps, warmup):
+    """The reference's own CPU path: ``AdamWReferenceSR.step`` of the unmodified
+    reference package (installed in baseline/_ref) on one 2^24-element tensor
+    with the config's formats (BF16 parameter and gradient, E4M3 stochastic
+    exp_avg, BF16 stochastic exp_avg_sq) and hyperparameters, all host threads.
+    Returns the per-step rates (params/s) and the thread count, or None when the
+    reference is not installed.  Must run before anything imports this
+    repository's own ``sr_states`` (the packages share the name)."""
+    if not (REFERENCE_DIR / "sr_states").is_dir():
+        return None
+    ours = str((ROOT / "stochastic-rounding-pytorch_b200").resolve())
+    sys.path[:] = [x for x in sys.path if str(Path(x or ".").resolve()) != ours]
+    sys.path.insert(0, str(REFERENCE_DIR))
+    import torch
+
+    import sr_states
+
+    if Path(sr_states.__file__).resolve().parents[1] != REFERENCE_DIR.resolve():
+        raise RuntimeError(f"expected the reference's sr_states, imported {sr_states.__file__}")
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(SEED)
+    p = torch.nn.Parameter((torch.randn(REFERENCE_SAMPLE, generator=gen) * 0.02)
+                           .to(torch.bfloat16))
+    p.grad = (torch.randn(REFERENCE_SAMPLE, generator=gen) * 1e-4).to(torch.bfloat16)
+    fmt = {"exp_avg": sr_states.StateFormat(torch.float8_e4m3fn, "stochastic"),
+           "exp_avg_sq": sr_states.StateFormat(torch.bfloat16, "stochastic")}
+    opt = sr_states.AdamWReferenceSR([p], lr=LR, betas=BETAS, eps=EPS,
+                                     weight_decay=WEIGHT_DECAY, state_format=fmt, seed=SEED)
+    rates = []
+    for i in range(warmup + steps):
+        t = time.perf_counter()
+        opt.step()
+        dt = time.perf_counter() - t
+        if i >= warmup:
+            rates.append(REFERENCE_SAMPLE / dt)
+    return rates, torch.get_num_threads()
+
+
+def reference_baseline_entry(rates, threads):
+    return {"value": statistics.median(rates), "unit": "params/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"median of {len(rates)} steps of the reference's AdamWReferenceSR.step "
+                      f"(unmodified package, baseline/_ref) on one {REFERENCE_SAMPLE}-element "
+                      "BF16 parameter with E4M3/BF16 stochastic states, "
+                      f"{sum(REFERENCE_SAMPLE / r for r in rates):.1f} s on {threads} threads; "
+                      "scaled to the config's parameters",
+            "spread": [min(rates), max(rates)]}
+
+
+def cpu_reference_subprocess(args):
+    """The reference CPU baseline measured in a fresh interpreter (this process
+    already imported this repository's ``sr_states``): the reference arm itself,
+    a few steps."""
+    import subprocess
+
+    if not (REFERENCE_DIR / "sr_states").is_dir():
+        return None
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT")}
+    out = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--impl", "reference",
+                          "--steps", "5", "--warmup", "1"], env=env, capture_output=True,
+                         text=True, timeout=900)
+    if out.returncode != 0:
+        return None
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    if not lines:
+        return None
+    entry = json.loads(lines[-1]).get("cpu_baseline")
+    if entry is not None:
+        entry.pop("port", None)
+    return entry
+
+
+# ----------------------------------------------------------- verification --
+
+VERIFY_WINDOW = 2048  # elements per sampled window
+
+
+def sample_windows(names, shapes, world, shard):
+    """Flat element windows [a, b) of the BF16 buffer whose update is checked:
+    both sides of every shard boundary, the head and tail of embed_tokens and
+    lm_head, the first layer's and the final RMSNorm vectors, and the middle of
+    a large matrix.  Merged where they overlap."""
+    offsets, at = {}, 0
+    for name, shape in zip(names, shapes):
+        offsets[name] = (at, math.prod(shape))
+        at += math.prod(shape)
+    total, half = at, VERIFY_WINDOW // 2
+    wanted = [(k * shard - half, k * shard + half) for k in range(1, world)]
+    for name in ("embed_tokens", "lm_head"):
+        if name in offsets:
+            start, n = offsets[name]
+            wanted += [(start, start + VERIFY_WINDOW), (start + n - VERIFY_WINDOW, start + n)]
+    for name in ("layers.0.input_layernorm", "norm"):
+        if name in offsets:
+            start, n = offsets[name]
+            wanted.append((start, start + n))
+    if "layers.0.gate_proj" in offsets:
+        start, n = offsets["layers.0.gate_proj"]
+        wanted.append((start + n // 2 - half, start + n // 2 + half))
+    merged = []
+    for a, b in sorted((max(0, a), min(total, b)) for a, b in wanted):
+        if a >= b:
+            continue
+        if merged and a <= merged[-1][1]:
+            merged[-1] = (merged[-1][0], max(b, merged[-1][1]))
+        else:
+            merged.append((a, b))
+    return merged, offsets
+
+
+def buffer_digest(buffer, n):
+    """Position-weighted checksum of the first n elements of a 16-bit buffer:
+    (sum of words, sum of (i+1) * word) mod 2^64, on the device in chunks."""
+    import torch
+
+    words = buffer.view(torch.int16)
+    chunk = 1 << 26
+    index = torch.arange(1, chunk + 1, dtype=torch.int64, device=buffer.device)
+    s1 = torch.zeros((), dtype=torch.int64, device=buffer.device)
+    s2 = torch.zeros((), dtype=torch.int64, device=buffer.device)
+    for a in range(0, n, chunk):
+        x = words[a:min(n, a + chunk)].to(torch.int64)
+        s1 += x.sum()
+        s2 += (x * (index[:x.numel()] + a)).sum()
+    return int(s1.item()), int(s2.item())
+
+
+def verify_step(opt, names, params, world, rank):
+    """One more optimizer step (untimed), checked two ways:
+
+    * every rank's replica of the flat BF16 parameters has the same digest
+      (the exchange delivered every shard everywhere);
+    * rank 0 recomputes sampled windows with the CPU oracle (the checker of the
+      tests) from the inputs of that step, gathered from the ranks that own
+      their optimizer states, and compares the parameter bytes of its own
+      replica and the states' bytes of their owners.
+    """
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from sr_states.distributed import shard_sizes
+
+    total = opt.flat_numel(torch.bfloat16)
+    shard = shard_sizes(total, world)
+    windows, offsets = sample_windows(names, [p.shape for p in params], world, shard)
+    index_of = {name: i for i, name in enumerate(names)}
+    segments = []  # (param index, lo, hi) within the parameter
+    for a, b in windows:
+        for name, (start, n) in offsets.items():
+            lo, hi = max(a, start) - start, min(b, start + n) - start
+            if lo < hi:
+                segments.append((index_of[name], lo, hi))
+
+    def bits(t, width):  # a copy, never a view of live memory
+        return t.detach().contiguous().view(width).cpu().numpy().copy()
+
+    def capture(with_params):
+        out = {}
+        for k, (i, lo, hi) in enumerate(segments):
+            p = params[i]
+            entry = {}
+            if with_params:
+                entry["p"] = bits(p.detach().reshape(-1)[lo:hi], torch.int16).view(np.uint16)
+                entry["g"] = bits(p.grad.reshape(-1)[lo:hi], torch.int16).view(np.uint16)
+            run = opt.local_run(p)
+            if run is not None and max(lo, run[0]) < min(hi, run[1]):
+                a, b = max(lo, run[0]), min(hi, run[1])
+                st = opt.state[p]
+                entry["run"] = (a, b)
+                entry["m"] = bits(st["exp_avg"][a - run[0]:b - run[0]], torch.uint8)
+                entry["v"] = bits(st["exp_avg_sq"][a - run[0]:b - run[0]],
+                                  torch.int16).view(np.uint16)
+                entry["step"] = int(st.get("step", 0))
+            out[k] = entry
+        return out
+
+    sync = torch.cuda.synchronize if torch.cuda.is_available() else (lambda: None)
+    sync()
+    before = capture(rank == 0)
+    opt.step()
+    sync()
+    after = capture(rank == 0)
+    digest = buffer_digest(opt.flat_params(torch.bfloat16), total)
+    rng_step = int(opt.param_groups[0]["sr_step"])
+    gathered = [None] * world
+    if world > 1:
+        dist.all_gather_object(gathered, (digest, before, after))
+    else:
+        gathered = [(digest, before, after)]
+    if rank != 0:
+        return None
+
+    import oracle
+
+    replicas_equal = all(d == gathered[0][0] for d, _, _ in gathered)
+    mismatched, checked = 0, 0
+    for k, (i, lo, hi) in enumerate(segments):
+        p = before[k]["p"].copy()
+        g = before[k]["g"]
+        m = np.zeros(hi - lo, np.uint8)
+        v = np.zeros(hi - lo, np.uint16)
+        m_after = np.zeros(hi - lo, np.uint8)
+        v_after = np.zeros(hi - lo, np.uint16)
+        owned = np.zeros(hi - lo, bool)
+        steps = set()
+        for _, b_r, a_r in gathered:
+            if "run" in b_r[k]:
+                a, b = b_r[k]["run"]
+                m[a - lo:b - lo], v[a - lo:b - lo] = b_r[k]["m"], b_r[k]["v"]
+                m_after[a - lo:b - lo], v_after[a - lo:b - lo] = a_r[k]["m"], a_r[k]["v"]
+                owned[a - lo:b - lo] = True
+                steps.add(a_r[k]["step"])
+        if not owned.all() or len(steps) != 1:
+            mismatched += 1 << 30  # a window nobody (or two steps) covered: fail loudly
+            continue
+        oracle.adamw_(p, g.copy(), m, v, m_fmt=oracle.E4M3, m_rule=oracle.STOCHASTIC,
+                      v_fmt=oracle.BF16, v_rule=oracle.STOCHASTIC, lr=LR, beta1=BETAS[0],
+                      beta2=BETAS[1], eps=EPS, weight_decay=WEIGHT_DECAY, step=steps.pop(),
+                      update_key=oracle.update_key(SEED, rng_step, i), offset=lo)
+        mismatched += int(np.count_nonzero(p.view(np.uint8) != after[k]["p"].view(np.uint8)))
+        mismatched += int(np.count_nonzero(m != m_after))
+        mismatched += int(np.count_nonzero(v.view(np.uint8) != v_after.view(np.uint8)))
+        checked += hi - lo
+    return {"replicas_equal": replicas_equal, "digest": list(gathered[0][0]),
+            "windows": len(windows), "rows": len(segments), "elements": checked,
+            "mismatched_bytes": mismatched, "rng_step": rng_step,
+            "checker": "CPU oracle (tests' checker) on sampled windows: both sides of every "
+                       "shard boundary, head and tail of embed_tokens and lm_head, two RMSNorm "
+                       "vectors, the middle of a matrix; p from rank 0's replica, m and v "
+                       "from their owners"}
 
 
 def e2e_run(opt, flat_p, flat_g, steps, world, total):
@@ -304,7 +552,31 @@ def e2e_run(opt, flat_p, flat_g, steps, world, total):
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
     return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms,
             "h2d_bytes_per_step": shard * 2, "d2h_bytes_per_step": shard * 2,
-            "api": "ZeroAdamW.step_host (pinned host gradients in, parameters out)"}
+            "api": "ZeroAdamW.step_host (pinned host gradients in, parameters out)" + (
+                f"; each of the {world} ranks loads its own gradient shard and sends back its "
+                "own updated parameter shard (bytes above are per rank)" if world > 1 else "")}
+
+
+def split_phase(opt, steps, world, stream):
+    """At N > 1: the same steps with the update and the exchange as separate
+    launches (the NCCL all-gather after the update), so the update alone and the
+    exchange alone are timed.  Nothing is skipped: the parameters that leave
+    these steps are the same as the fused exchange's."""
+    import torch
+
+    connected = opt.gather_mode
+    opt.set_gather_mode("nccl")
+    try:
+        opt.step()  # warm-up of the NCCL path
+        torch.cuda.synchronize()
+        opt.timings.clear()
+        time_steps(opt, steps, world, stream)
+        timings = list(opt.timings)
+        opt.timings.clear()
+    finally:
+        opt.set_gather_mode(connected)
+    return (max_over_ranks(statistics.mean(t["update_ms"] for t in timings), world),
+            max_over_ranks(statistics.mean(t["gather_ms"] for t in timings), world))
 
 
 def run_b200(args):
@@ -312,9 +584,8 @@ def run_b200(args):
 
     world, rank = init_distributed(args.gpus)
     peak, peak_source = measured_hbm_peak()
-    opt, params, flat_p, flat_g, total = build_workload(world, rank, args.layers,
-                                                        not args.no_embeddings, args.gather,
-                                                        args.chunks)
+    opt, names, params, flat_p, flat_g, total = build_workload(
+        world, rank, args.layers, not args.no_embeddings, args.gather, args.chunks)
     local = opt.local_numel()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -325,14 +596,21 @@ def run_b200(args):
         total_ms, per_step = time_steps(opt, args.steps, world, stream)
     total_ms = max_over_ranks(total_ms, world)
     ms = total_ms / args.steps
-    kernel_ms = max_over_ranks(statistics.mean(t["update_ms"] for t in opt.timings), world)
-    gather_ms = max_over_ranks(statistics.mean(t.get("gather_ms", 0.0) for t in opt.timings),
-                               world)
-    achieved = BYTES_PER_PARAM * local / (kernel_ms / 1e3) / 1e9
+    step_kernel_ms = max_over_ranks(statistics.mean(t["update_ms"] for t in opt.timings), world)
+    barrier_ms = max_over_ranks(statistics.mean(t.get("gather_ms", 0.0) for t in opt.timings),
+                                world)
+    opt.timings.clear()
+    if world > 1:
+        update_ms, nccl_ms = split_phase(opt, args.steps, world, stream)
+    else:
+        update_ms, nccl_ms = step_kernel_ms, None
+    achieved = BYTES_PER_PARAM * local / (update_ms / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": total / (ms / 1e3), "unit": "params/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "dtype_meaning": "arithmetic of the update (FP32 math); storage: BF16 parameters and "
+                         "gradients, FP8 E4M3 exp_avg, BF16 exp_avg_sq",
         "data": "synthetic",
         "config": {"workload": "llama3-8b AdamW-SR optimizer step (BASELINE config 4)"
                    + ("" if (args.layers, args.no_embeddings) == (32, False)
@@ -355,16 +633,35 @@ def run_b200(args):
                      "traffic_source": "ncu dram bytes per parameter of the 2-layer case, "
                                        "scaled to this launch",
                      "peak_source": peak_source,
-                     "kernel": "srs::adamw_kernel<E4M3,BF16>", "kernel_ms": kernel_ms,
+                     "kernel": "srs::adamw_kernel<E4M3,BF16>", "kernel_ms": update_ms,
+                     "timed": "the update launch alone" + (
+                         " (from the steps whose exchange is a separate NCCL all-gather)"
+                         if world > 1 else ""),
                      "bytes_per_param": BYTES_PER_PARAM, "params_per_launch": local},
-        "gather_ms": gather_ms if world > 1 else 0.0,
         "step_ms_min": min(per_step), "gpu_launches": opt.launches_per_step() * args.steps,
         "clocks": clocks.report(),
     }
+    if world > 1:
+        received = (world - 1) * local * 2  # BF16 bytes every GPU receives per step
+        line["exchange"] = {
+            "mechanism": opt.gather_mode, "bytes_received_per_gpu": received,
+            "step_kernel_ms": step_kernel_ms, "barriers_ms": barrier_ms,
+            "receive_gbs": received / (ms / 1e3) / 1e9,
+            "bound_gbs": NVLINK_PEER_GBS,
+            "frac": received / (ms / 1e3) / 1e9 / NVLINK_PEER_GBS,
+            "bound_source": "measured peer copy per direction and GPU (copy engines); "
+                            "nominal NVLink 5: 900 GB/s",
+            "receive_bound_ms": received / (NVLINK_PEER_GBS * 1e9) * 1e3,
+            "update_alone_ms": update_ms, "nccl_allgather_ms": nccl_ms,
+            "nccl_allgather_gbs": received / (nccl_ms / 1e3) / 1e9}
+    line["verify"] = verify_step(opt, names, params, world, rank)
+    if rank != 0:
+        line.pop("verify")
     if not args.no_e2e:
         line["e2e"] = e2e_run(opt, flat_p, flat_g, args.e2e_steps, world, total)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        line["cpu_baseline"] = cpu_reference_subprocess(args) or cpu_baseline(args.cpu_seconds)
+        line["cpu_baseline"]["port"] = cpu_baseline(min(args.cpu_seconds, 4.0))
     if rank == 0:
         print(json.dumps(line), flush=True)
     opt.close()
@@ -607,16 +904,23 @@ def run_adamw_70b(args):
 
 
 def run_reference(args):
-    """The reference arm: the CPU restatement of the reference algorithm (the reference
-    itself is Python on PyTorch's CPU kernels and does not travel to this box) on all
-    host cores; every step is a bounded sample of the same workload."""
+    """The reference arm: the reference's own CPU implementation of the step
+    (``AdamWReferenceSR.step`` of the unmodified package in baseline/_ref) on
+    all host cores; every step is a 2^24-element sample of the workload, the
+    rate scaled to its 8,030,261,248 parameters.  Without the installed
+    reference, the C restatement of the algorithm (the tests' oracle) stands in,
+    labelled ``kind: port``.  Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    samples = [cpu_baseline(args.cpu_seconds / max(args.steps, 1))
-               for _ in range(args.warmup + args.steps)][args.warmup:]
-    value = statistics.median(s["value"] for s in samples)
-    base = dict(samples[-1], value=value)
+    measured = reference_cpu_steps(args.steps, args.warmup)
+    if measured is not None:
+        base = reference_baseline_entry(*measured)
+    else:
+        samples = [cpu_baseline(max(1.0, args.cpu_seconds / max(args.steps, 1)))
+                   for _ in range(args.steps)]
+        base = dict(samples[-1], value=statistics.median(s["value"] for s in samples))
+    value = base["value"]
     print(json.dumps({
         "metric": METRIC, "impl": "reference", "value": value, "unit": "params/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -627,8 +931,8 @@ def run_reference(args):
                    "grad_dtype": "bf16", "exp_avg": "float8_e4m3fn stochastic",
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": "host cores",
                    "global_batch": None, "seq_len": None,
-                   "timing": "each step a bounded sample of the workload, scaled to its "
-                             "8,030,261,248 parameters (see cpu_baseline.sample)"},
+                   "timing": "each step a 2^24-element sample of the workload; ms_per_step "
+                             "extrapolated to its 8,030,261,248 parameters"},
         "cpu_baseline": base,
         "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0}}), flush=True)

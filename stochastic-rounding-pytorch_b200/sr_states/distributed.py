@@ -604,6 +604,16 @@ class _ZeroMixin:
             self._events.append(marks)
         return loss
 
+    def local_run(self, p) -> tuple[int, int] | None:
+        """[lo, hi) of p's flattened elements that this rank updates (its states
+        hold exactly these elements), or None."""
+        return self._layout.local_run(p)
+
+    def flat_params(self, dtype):
+        """This rank's replica of the flat parameter buffer of a dtype (padded
+        to equal shards; element i is flat parameter element i)."""
+        return self._layout.buffers[dtype]
+
     def flat_grads(self, dtype):
         """The flat gradient buffer of a parameter dtype (``grads="reduce_scatter"``;
         None otherwise): element i is the gradient of flat parameter element i."""

@@ -4,6 +4,9 @@ this package's optimizer classes and compare every step with the reference bytes
 Parameters are teacher-forced: after each step's comparison the parameter is
 reset to the reference's bytes, so a one-ulp difference (PyTorch's CPU sqrt is
 not correctly rounded) never compounds.  States never depend on parameters.
+AdamW parameters are checked with the reference's own intermediates of each
+update (tests/golden/optimizers_intermediates.npz): equal to its update formula
+evaluated with a correctly rounded square root, byte for byte.
 """
 
 from __future__ import annotations
@@ -11,8 +14,9 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from _support import (FMT, adamw_param_close, assert_bits_or_nan, from_bits, load_json, load_npz,
-                      tbits, ulp_distance)
+import oracle
+from _support import (FMT, assert_bits_or_nan, explain_adamw_param, from_bits, load_json,
+                      load_npz, tbits, ulp_distance)
 
 
 def scenarios():
@@ -57,6 +61,7 @@ def build(spec, arrays, device, cls=None):
 def replay(spec, device, cls=None, arrays=None):
     """Run the scenario; returns (total parameter elements compared, mismatching ones)."""
     arrays = arrays if arrays is not None else load_npz("optimizers.npz")
+    intermediates = load_npz("optimizers_intermediates.npz")
     name, names, kind = spec["name"], spec["state_names"], spec["kind"]
     params, opt = build(spec, arrays, device, cls)
     skip = {tuple(x) for x in spec["grad_none"]}
@@ -76,13 +81,19 @@ def replay(spec, device, cls=None, arrays=None):
             distance = ulp_distance(actual, golden, width)
             if kind == "sgdm":
                 assert distance.max(initial=0) == 0, context
-            else:
+            elif f"{name}__p{i}__sqrt{step}" in intermediates:
                 hp = group_of[i]["hp"]
                 prev = (previous[i].view(np.float32) if width == 32
                         else (previous[i].astype(np.uint32) << 16).view(np.float32))
-                ok = adamw_param_close(actual, golden, prev, 1.0 - hp["lr"] * hp["weight_decay"],
-                                       width)
-                assert ok.all(), f"{context}: {distance.max()} ulp"
+                beta1, beta2 = hp.get("betas", (0.9, 0.999))
+                adam_step = int(arrays[f"{name}__p{i}__adamstep{step}"][0])
+                scalars = oracle.adamw_scalars(hp["lr"], beta1, beta2, hp.get("eps", 1e-8),
+                                               hp.get("weight_decay", 1e-2), adam_step)
+                inter = [intermediates[f"{name}__p{i}__{k}{step}"].view(np.float32)
+                         for k in ("v32", "sqrt", "m32")]
+                explain_adamw_param(actual, golden, prev, *inter, scalars, width)
+            else:  # no update this step (no gradient): unchanged
+                assert distance.max(initial=0) == 0, context
             compared += distance.size
             mismatched += int(np.count_nonzero(distance))
             for n in names:

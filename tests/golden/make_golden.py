@@ -13,6 +13,10 @@ outputs on seeded synthetic inputs:
   functional.npz   adamw_step_ / sgdm_step_ on one tensor at offset 2^32-211
   config1.npz      BASELINE config 1 (AdamW, FP32 param, BF16 SR states, 10 steps) at
                    n = 2^13, every step's bytes
+  config1_intermediates.npz  the reference's own v32, v32.sqrt() and m32 of every step
+                   of that run (where its CPU sqrt is not correctly rounded)
+  optimizers_intermediates.npz  the same intermediates for every AdamW update of
+                   the optimizer scenarios below
   config1_full.json  the same run at n = 2^20: SHA-256 of the state bytes after each step
   optimizers.npz / optimizers.json
                    multi-parameter, multi-group optimizer scenarios (param_index, RNG
@@ -284,6 +288,77 @@ def run_config1(ref, n, steps=10, record_all=True):
     return arrays, digests
 
 
+class _SqrtRecorder:
+    """Records the FP32 intermediates of the reference's AdamW update while active:
+    the input and output of its square root (``v32.sqrt()``,
+    sr_states/reference/adamw.py:86) and the first moment m32 it passes to
+    ``addcdiv_`` (:88)."""
+
+    def __init__(self):
+        import torch
+
+        self.seen = {}
+        self._torch = torch
+        self._saved = None
+
+    def __enter__(self):
+        torch = self._torch
+        real_sqrt, real_addcdiv = torch.Tensor.sqrt, torch.Tensor.addcdiv_
+        seen = self.seen
+
+        def sqrt(tensor):
+            out = real_sqrt(tensor)
+            seen["v32"], seen["sqrt"] = tensor.detach().clone(), out.detach().clone()
+            return out
+
+        def addcdiv_(tensor, tensor1, tensor2, *args, **kwargs):
+            seen["m32"] = tensor1.detach().clone()
+            return real_addcdiv(tensor, tensor1, tensor2, *args, **kwargs)
+
+        self._saved = (real_sqrt, real_addcdiv)
+        torch.Tensor.sqrt, torch.Tensor.addcdiv_ = sqrt, addcdiv_
+        return self
+
+    def __exit__(self, *exc):
+        self._torch.Tensor.sqrt, self._torch.Tensor.addcdiv_ = self._saved
+        return False
+
+
+def record_adamw_intermediates(opt, params, sink):
+    """Wrap ``opt._step_parameter`` so that each parameter update stores the
+    reference's intermediates in ``sink[param index]`` (a fresh dict per update)."""
+    original = opt._step_parameter
+    index = {id(p): i for i, p in enumerate(params)}
+
+    def step_parameter(parameter, *args, **kwargs):
+        with _SqrtRecorder() as recorder:
+            original(parameter, *args, **kwargs)
+        sink[index[id(parameter)]] = dict(recorder.seen)
+
+    opt._step_parameter = step_parameter
+
+
+def run_config1_intermediates(ref, n, steps=10):
+    """The same run as run_config1, recording the reference's own FP32
+    intermediates of every step (see _SqrtRecorder).  PyTorch's CPU sqrt is not
+    correctly rounded, and these bytes show exactly where it differs."""
+    import torch
+
+    gen = torch.Generator().manual_seed(1234)
+    p = torch.nn.Parameter(torch.randn(n, generator=gen) * 0.02)
+    opt = ref.AdamWReferenceSR([p], lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                               state_dtype=torch.bfloat16, rounding="stochastic", seed=7)
+    arrays, sink = {}, {}
+    record_adamw_intermediates(opt, [p], sink)
+    for step in range(1, steps + 1):
+        p.grad = torch.randn(n, generator=gen) * 1e-3
+        sink.clear()
+        opt.step()
+        for name in ("v32", "sqrt", "m32"):
+            arrays[f"{name}_{step}"] = bits(sink[0][name])
+    return arrays
+
+
 # ------------------------------------------------------------- optimizers --
 
 def _scenario(ref, name, kind, groups, shapes, steps, grad_none=(), initial=None, init_seed=0,
@@ -325,6 +400,9 @@ def _scenario(ref, name, kind, groups, shapes, steps, grad_none=(), initial=None
             arrays[f"{name}__p{pid}__{n}__init"] = bits(st[n])
         st["step"] = spec["step"]
     skip = {tuple(x) for x in grad_none}
+    sink = {}
+    if kind == "adamw":
+        record_adamw_intermediates(opt, params, sink)
     for step in range(1, steps + 1):
         for i, p in enumerate(params):
             if (step, i) in skip:
@@ -332,7 +410,11 @@ def _scenario(ref, name, kind, groups, shapes, steps, grad_none=(), initial=None
             else:
                 p.grad = (torch.randn(p.shape, generator=gen) * grad_scale).to(p.dtype)
                 arrays[f"{name}__p{i}__grad{step}"] = bits(p.grad)
+        sink.clear()
         opt.step()
+        for i, seen in sink.items():
+            for key in ("v32", "sqrt", "m32"):
+                arrays[f"{name}__p{i}__{key}{step}"] = bits(seen[key])
         for i, p in enumerate(params):
             arrays[f"{name}__p{i}__step{step}"] = bits(p)
             for n in names:
@@ -482,12 +564,17 @@ def make_regression(ref):
     return arrays, cases
 
 
+def _is_intermediate(key: str) -> bool:
+    tail = key.rsplit("__", 1)[-1]
+    return tail.startswith(("v32", "sqrt", "m32"))
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--reference", default=os.environ.get("SR_STATES_REFERENCE"),
                         help="checkout of the reference (default: $SR_STATES_REFERENCE)")
-    parser.add_argument("--only", choices=("regression",), default=None,
-                        help="write one fixture family only")
+    parser.add_argument("--only", choices=("regression", "intermediates"),
+                        default=None, help="write one fixture family only")
     args = parser.parse_args()
     if not args.reference:
         parser.error("give --reference or set SR_STATES_REFERENCE")
@@ -500,6 +587,13 @@ def main():
     meta = {"generator": "tests/golden/make_golden.py", "torch": str(torch.__version__),
             "reference_version": getattr(ref, "__version__", "?")}
 
+    if args.only == "intermediates":
+        np.savez_compressed(HERE / "config1_intermediates.npz",
+                            **run_config1_intermediates(ref, 1 << 13))
+        arrays, _ = make_optimizers(ref)
+        np.savez_compressed(HERE / "optimizers_intermediates.npz",
+                            **{k: v for k, v in arrays.items() if _is_intermediate(k)})
+        return
     arrays, cases = make_regression(ref)
     np.savez_compressed(HERE / "regression.npz", **arrays)
     (HERE / "regression.json").write_text(json.dumps({"meta": meta, "cases": cases}, indent=1))
@@ -514,10 +608,14 @@ def main():
     (HERE / "functional.json").write_text(json.dumps({"meta": meta, "cases": manifest}, indent=1))
     arrays, _ = run_config1(ref, 1 << 13)
     np.savez_compressed(HERE / "config1.npz", **arrays)
+    np.savez_compressed(HERE / "config1_intermediates.npz",
+                        **run_config1_intermediates(ref, 1 << 13))
     _, digests = run_config1(ref, 1 << 20, record_all=False)
     (HERE / "config1_full.json").write_text(json.dumps(
         {"meta": meta, "n": 1 << 20, "seed_generator": 1234, "steps": digests}, indent=1))
     arrays, specs = make_optimizers(ref)
+    intermediates = {k: arrays.pop(k) for k in list(arrays) if _is_intermediate(k)}
+    np.savez_compressed(HERE / "optimizers_intermediates.npz", **intermediates)
     np.savez_compressed(HERE / "optimizers.npz", **arrays)
     (HERE / "optimizers.json").write_text(json.dumps({"meta": meta, "scenarios": specs},
                                                      indent=1))

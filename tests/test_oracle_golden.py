@@ -8,7 +8,7 @@ import pytest
 
 import _scenarios
 import oracle
-from _support import adamw_param_close, load_json, load_npz, ulp_distance
+from _support import explain_adamw_param, load_json, load_npz, ulp_distance
 
 
 def test_update_and_state_keys_match_reference():
@@ -78,25 +78,32 @@ def _config1_step(p, g, m, v, step):
 
 def test_oracle_config1_trajectory_matches_reference():
     """BASELINE config 1 at n = 2^13: every step teacher-forced from the reference's
-    previous bytes; states bit-exact, FP32 parameter within the sqrt tolerance."""
+    previous bytes.  States bit-exact; the FP32 parameter equals the reference's
+    update formula with a correctly rounded square root, byte for byte, so it is
+    byte-exact wherever the reference's CPU sqrt is correctly rounded and every
+    other difference is that sqrt's (tests/golden/config1_intermediates.npz)."""
     a = load_npz("config1.npz")
+    inter = load_npz("config1_intermediates.npz")
     p = a["param_init"].view(np.float32).copy()
     m = np.zeros(p.size, np.uint16)
     v = np.zeros(p.size, np.uint16)
-    mismatched = 0
+    roots, params, worst = 0, 0, 0
     for step in range(1, 11):
         g = a[f"grad_{step}"].view(np.float32).copy()
         _config1_step(p, g, m, v, step)
         assert np.array_equal(m, a[f"exp_avg_{step}"]), step
         assert np.array_equal(v, a[f"exp_avg_sq_{step}"]), step
         p_prev = a["param_init" if step == 1 else f"param_{step - 1}"].view(np.float32)
-        assert adamw_param_close(p.view(np.uint32), a[f"param_{step}"], p_prev,
-                                 1.0 - 3e-4 * 0.01, 32).all(), step
-        mismatched += int(np.count_nonzero(p.view(np.uint32) != a[f"param_{step}"]))
+        scalars = oracle.adamw_scalars(3e-4, 0.9, 0.999, 1e-8, 0.01, step)
+        r, d, w = explain_adamw_param(
+            p.view(np.uint32), a[f"param_{step}"], p_prev,
+            *(inter[f"{k}_{step}"].view(np.float32) for k in ("v32", "sqrt", "m32")),
+            scalars, 32)
+        roots, params, worst = roots + r, params + d, max(worst, w)
         p = a[f"param_{step}"].view(np.float32).copy()
-    # PyTorch's CPU sqrt differs from a correctly rounded one on ~0.7% of inputs;
-    # ~1e-4 of parameters then differ by one ulp.
-    assert mismatched / (10 * p.size) < 2e-3
+    # Measured: 550 of 81,920 roots differ, 13 parameters, at most 2 ulp.
+    print(f"config 1: {roots} roots and {params} parameters differ, max {worst} ulp")
+    assert roots > 0 and params <= roots
 
 
 def test_oracle_config1_full_size_state_digests():

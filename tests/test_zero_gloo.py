@@ -334,3 +334,79 @@ def test_zero_never_adopts_storage_shared_with_other_tensors():
     a fresh flat buffer, so the padding's all-gather cannot overwrite that tensor."""
     results = _spawn(_shared_storage_worker, 2)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def _verify_worker(rank, world, port, queue):
+    sys.path[:0] = [str(ROOT), str(ROOT / "stochastic-rounding-pytorch_b200"), str(ROOT / "tests")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import importlib.util
+    import math
+
+    import torch.distributed as dist
+
+    from _support import FakeLauncher
+    from sr_states import StateFormat
+    from sr_states.cuda import _native
+    from sr_states.distributed import ZeroAdamW
+    from sr_states.shapes import _llama
+
+    class CorruptingLauncher(FakeLauncher):
+        """The oracle stand-in, plus one wrong first-moment byte on rank 1: a
+        planted mistake that the bench's verification must report."""
+
+        def adamw_multi(self, table, *args, **kwargs):
+            super().adamw_multi(table, *args, **kwargs)
+            if rank == 1:
+                address = int(table.host[0]["state"][0])
+                byte = (ctypes.c_uint8 * 1).from_address(address)
+                byte[0] ^= 0x01
+
+    import ctypes
+
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+        bench = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(bench)
+        named = _llama(2, 64, 16, 128, vocab=300)
+        names, shapes = [n for n, _ in named], [s for _, s in named]
+        results = []
+        for launcher in (FakeLauncher(), CorruptingLauncher()):
+            _native.set_launcher(launcher)
+            gen = torch.Generator().manual_seed(7)
+            params = [torch.nn.Parameter((torch.randn(math.prod(s), generator=gen) * 0.02)
+                                         .to(torch.bfloat16).view(s)) for s in shapes]
+            fmt = {"exp_avg": StateFormat(torch.float8_e4m3fn, "stochastic"),
+                   "exp_avg_sq": StateFormat(torch.bfloat16, "stochastic")}
+            opt = ZeroAdamW(params, lr=bench.LR, betas=bench.BETAS, eps=bench.EPS,
+                            weight_decay=bench.WEIGHT_DECAY, state_format=fmt, seed=bench.SEED,
+                            grads="reduce_scatter")
+            opt.flat_grads(torch.bfloat16).copy_(
+                torch.randn(opt.flat_grads(torch.bfloat16).numel(), generator=gen) * 1e-4)
+            for _ in range(2):
+                opt.step()
+            results.append(bench.verify_step(opt, names, params, world, rank))
+        if rank == 0:
+            clean, corrupt = results
+            assert clean["replicas_equal"] and clean["mismatched_bytes"] == 0, clean
+            assert clean["elements"] > 0 and clean["rng_step"] == 3, clean
+            assert corrupt["mismatched_bytes"] > 0, corrupt
+        else:
+            assert results == [None, None]
+        queue.put((rank, "ok"))
+    except BaseException:  # report, never hang the parent
+        import traceback
+        queue.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_bench_verification_passes_sharded_steps_and_reports_a_planted_mistake():
+    """bench.py's post-run check (replica digests plus oracle windows gathered
+    from the owners of the states) on two gloo ranks: clean steps verify, and a
+    wrong state byte on one rank is reported."""
+    results = _spawn(_verify_worker, 2)
+    assert results == {0: "ok", 1: "ok"}, results
