@@ -328,10 +328,17 @@ template <> struct Fmt<SRS_FMT_E5M2> { static constexpr int kBytes = 1; };
 
 template <int F> constexpr int kWords = kVec * Fmt<F>::kBytes / 4;
 
+// Element offsets (e0) are int64_t or uint32_t: a uint32_t offset, zero-extended,
+// lets the address be one wide multiply-add (the staged loops use it).
+template <int F, typename I>
+__device__ __forceinline__ const char* elem_ptr(const void* base, I e0) {
+  return static_cast<const char*>(base) + static_cast<size_t>(e0) * Fmt<F>::kBytes;
+}
+
 // Raw 8-element load (16-byte aligned for 2- and 4-byte formats, 8-byte for FP8).
-template <int F>
-__device__ __forceinline__ void load_raw8(const void* base, int64_t e0, uint32_t (&w)[kWords<F>]) {
-  const char* p = static_cast<const char*>(base) + e0 * Fmt<F>::kBytes;
+template <int F, typename I>
+__device__ __forceinline__ void load_raw8(const void* base, I e0, uint32_t (&w)[kWords<F>]) {
+  const char* p = elem_ptr<F>(base, e0);
   if constexpr (kWords<F> == 8) {
     const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
     const uint4 b = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
@@ -346,9 +353,9 @@ __device__ __forceinline__ void load_raw8(const void* base, int64_t e0, uint32_t
   }
 }
 
-template <int F>
-__device__ __forceinline__ void store_raw8(void* base, int64_t e0, const uint32_t (&w)[kWords<F>]) {
-  char* p = static_cast<char*>(base) + e0 * Fmt<F>::kBytes;
+template <int F, typename I>
+__device__ __forceinline__ void store_raw8(void* base, I e0, const uint32_t (&w)[kWords<F>]) {
+  char* p = const_cast<char*>(elem_ptr<F>(base, e0));
   if constexpr (kWords<F> == 8) {
     __stcs(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
     __stcs(reinterpret_cast<uint4*>(p) + 1, make_uint4(w[4], w[5], w[6], w[7]));
@@ -368,8 +375,8 @@ __device__ __forceinline__ uint32_t raw_element(const uint32_t (&w)[kWords<F>], 
 }
 
 // Guarded scalar load of `count` (< 8 or unaligned) elements into packed words.
-template <int F>
-__device__ __forceinline__ void load_raw_partial(const void* base, int64_t e0, int count,
+template <int F, typename I>
+__device__ __forceinline__ void load_raw_partial(const void* base, I e0, int count,
                                                  uint32_t (&w)[kWords<F>]) {
 #pragma unroll
   for (int i = 0; i < kWords<F>; ++i) w[i] = 0u;
@@ -387,8 +394,8 @@ __device__ __forceinline__ void load_raw_partial(const void* base, int64_t e0, i
   }
 }
 
-template <int F>
-__device__ __forceinline__ void store_raw_partial(void* base, int64_t e0, int count,
+template <int F, typename I>
+__device__ __forceinline__ void store_raw_partial(void* base, I e0, int count,
                                                   const uint32_t (&w)[kWords<F>]) {
 #pragma unroll
   for (int j = 0; j < kVec; ++j) {
@@ -584,8 +591,8 @@ __device__ __forceinline__ void encode8(const float (&x)[kVec], uint32_t ctr0, i
 // ------------------------------------------------------ parameter dtypes --
 
 // Parameters and gradients are FP32 (P_BF16 == false) or BF16.
-template <bool BF16>
-__device__ __forceinline__ void load_param8(const void* base, int64_t e0, int count, bool vec,
+template <bool BF16, typename I>
+__device__ __forceinline__ void load_param8(const void* base, I e0, int count, bool vec,
                                             float (&x)[kVec]) {
   if constexpr (BF16) {
     uint32_t w[4];
@@ -603,8 +610,8 @@ __device__ __forceinline__ void load_param8(const void* base, int64_t e0, int co
 // Parameter write-back: FP32 as is, BF16 round-to-nearest-even.  With peers,
 // the same bytes also go to the same offset of every peer's replica (plain
 // stores through the peer mappings: the fused all-gather of a sharded step).
-template <bool BF16>
-__device__ __forceinline__ void store_param8(void* base, int64_t e0, int count, bool vec,
+template <bool BF16, typename I>
+__device__ __forceinline__ void store_param8(void* base, I e0, int count, bool vec,
                                              const float (&x)[kVec],
                                              const srs_peers* peers = nullptr) {
   constexpr int F = BF16 ? SRS_FMT_BF16 : SRS_FMT_F32;
@@ -622,8 +629,8 @@ __device__ __forceinline__ void store_param8(void* base, int64_t e0, int count, 
   }
 }
 
-template <int F>
-__device__ __forceinline__ void load_state8(const void* base, int64_t e0, int count, bool vec,
+template <int F, typename I>
+__device__ __forceinline__ void load_state8(const void* base, I e0, int count, bool vec,
                                             float (&x)[kVec]) {
   uint32_t w[kWords<F>];
   if (vec) load_raw8<F>(base, e0, w);
@@ -631,8 +638,8 @@ __device__ __forceinline__ void load_state8(const void* base, int64_t e0, int co
   decode8<F>(w, x);
 }
 
-template <int F>
-__device__ __forceinline__ void store_state8(void* base, int64_t e0, int count, bool vec,
+template <int F, typename I>
+__device__ __forceinline__ void store_state8(void* base, I e0, int count, bool vec,
                                              const float (&x)[kVec], uint32_t ctr0,
                                              int rule) {
   uint32_t w[kWords<F>];
@@ -645,8 +652,8 @@ __device__ __forceinline__ void store_state8(void* base, int64_t e0, int count, 
 // for the FP16/FP8 grids |x| < 2^63): the stochastic rule goes straight to the
 // fast form.  Only the stochastic and nearest rules come here (toward-zero
 // states take store_state8), which keeps the hot loops free of that code.
-template <int F>
-__device__ __forceinline__ void store_state8_screened(void* base, int64_t e0, int count, bool vec,
+template <int F, typename I>
+__device__ __forceinline__ void store_state8_screened(void* base, I e0, int count, bool vec,
                                                       const float (&x)[kVec], uint32_t ctr0,
                                                       bool stochastic) {
   uint32_t w[kWords<F>];

@@ -172,7 +172,14 @@ struct Stage {
   static constexpr int kS1 = S1 >= 0 ? kVec * Fmt<(S1 >= 0 ? S1 : 0)>::kBytes : 0;
   static constexpr int kBytes = kThreads * (kP + kG + kS0 + kS1);
 };
-constexpr int kStages = 2;
+#ifndef SRS_STAGES
+#define SRS_STAGES 2
+#endif
+constexpr int kStages = SRS_STAGES;
+// Rows the staged loops take: element offsets within them fit in 32 bits (the
+// RNG contract limits a parameter to 2^32 elements; longer rows of the C ABI
+// run the generic path).
+constexpr uint32_t kMaxStagedRow = 0xFFFFFFFFu;
 
 template <int BYTES>
 __device__ __forceinline__ void cp_async_chunk(uint32_t s, const void* g) {
@@ -198,19 +205,22 @@ __device__ __forceinline__ void cp_async_wait_stage() {
 }
 
 // Copies of this thread's chunks of the tile whose thread-0 element is e0 - threadIdx.x*8.
+// e0 is a uint32_t element offset within the row (rows of the staged loops hold
+// at most 2^32 elements), so each address is one wide multiply-add.
 template <int PBYTES, int GBYTES, int S0, int S1>
-__device__ __forceinline__ void stage_issue(const RowView& rv, int64_t e0, char* stage) {
+__device__ __forceinline__ void stage_issue(const RowView& rv, uint32_t e0, char* stage) {
   using S = Stage<PBYTES, GBYTES, S0, S1>;
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(stage);
   const uint32_t t = threadIdx.x;
-  cp_async_chunk<S::kP>(base + t * S::kP, static_cast<const char*>(rv.p) + e0 * PBYTES);
+  const size_t e = e0;
+  cp_async_chunk<S::kP>(base + t * S::kP, static_cast<const char*>(rv.p) + e * PBYTES);
   cp_async_chunk<S::kG>(base + kThreads * S::kP + t * S::kG,
-                        static_cast<const char*>(rv.g) + e0 * GBYTES);
+                        static_cast<const char*>(rv.g) + e * GBYTES);
   cp_async_chunk<S::kS0>(base + kThreads * (S::kP + S::kG) + t * S::kS0,
-                         static_cast<const char*>(rv.s0) + e0 * Fmt<S0>::kBytes);
+                         static_cast<const char*>(rv.s0) + e * Fmt<S0>::kBytes);
   if constexpr (S1 >= 0)
     cp_async_chunk<S::kS1>(base + kThreads * (S::kP + S::kG + S::kS0) + t * S::kS1,
-                           static_cast<const char*>(rv.s1) + e0 * Fmt<S1>::kBytes);
+                           static_cast<const char*>(rv.s1) + e * Fmt<S1>::kBytes);
 }
 
 // This thread's chunk of array `block` (0 = parameter, 1 = gradient, 2, 3 = states).
@@ -335,17 +345,21 @@ __device__ __forceinline__ void adamw_update_fast(float (&p)[kVec], const float 
     const float2 nq0 = mul2_rn(n2, ny1);
     const float2 res = fma2_rn(den, nq0, n2);
     const float2 nq = fma2_rn(res, ny1, nq0);  // -(num / den)
-    // Scalar, like mul_add_rn2: a packed p*decay feeding a packed add or sub is
-    // contracted into one FMA by ptxas (even written as fma(p, decay, -0)).
-    p[2 * i] = __fadd_rn(__fmul_rn(p[2 * i], decay.x), -nq.x);
-    p[2 * i + 1] = __fadd_rn(__fmul_rn(p[2 * i + 1], decay.y), -nq.y);
+    // p*decay rounded, then RN(pd - nq) as an FMA with multiplier -1: a packed
+    // product feeding a packed add or sub would be contracted into one FMA by
+    // ptxas (even written as fma(p, decay, -0)), a product feeding an FMA's
+    // addend cannot be.  Checked bit for bit against the oracle.
+    const float2 pd = mul2_rn(make_float2(p[2 * i], p[2 * i + 1]), decay);
+    const float2 p1 = fma2_rn(nq, splat(-1.0f), pd);
+    p[2 * i] = p1.x;
+    p[2 * i + 1] = p1.y;
   }
 }
 
 // Loads of one thread's 8 elements and the moment updates (every path):
 //   m' = fma(g, 1-b1, m*b1); v' = fma((1-b2)*g, g, v*b2).
-template <bool PB, bool GB, int MF, int VF, bool VEC>
-__device__ __forceinline__ void adamw_moments(const RowView& rv, int64_t e0, int count,
+template <bool PB, bool GB, int MF, int VF, bool VEC, typename I>
+__device__ __forceinline__ void adamw_moments(const RowView& rv, I e0, int count,
                                               const AdamWArgs& a, float (&p)[kVec],
                                               float (&m)[kVec], float (&v)[kVec]) {
   float g[kVec];
@@ -372,8 +386,8 @@ __device__ __forceinline__ void adamw_moments(const RowView& rv, int64_t e0, int
 // Out of line: it runs for vectors outside the screen, which are rare, and it
 // reloads its inputs (nothing is stored before the screen's decision) so that
 // the screened path keeps its values in registers.
-template <bool PB, bool GB, int MF, int VF, bool VEC>
-__device__ __noinline__ void adamw8_exact(const RowView& rv, int64_t e0, int count,
+template <bool PB, bool GB, int MF, int VF, bool VEC, typename I>
+__device__ __noinline__ void adamw8_exact(const RowView& rv, I e0, int count,
                                           const ClassScalars& k, const AdamWArgs& a) {
   float p[kVec], m[kVec], v[kVec];
   adamw_moments<PB, GB, MF, VF, VEC>(rv, e0, count, a, p, m, v);
@@ -397,8 +411,8 @@ __device__ __noinline__ void adamw8_exact(const RowView& rv, int64_t e0, int cou
 // Moments, screen and update of one thread's 8 loaded elements, then the
 // stores; vectors outside the screen (or classes without the screened
 // arithmetic) are redone by adamw8_exact from global memory.
-template <bool PB, bool GB, int MF, int VF, bool VEC>
-__device__ __forceinline__ void adamw8_compute(const RowView& rv, int64_t e0, int count,
+template <bool PB, bool GB, int MF, int VF, bool VEC, typename I>
+__device__ __forceinline__ void adamw8_compute(const RowView& rv, I e0, int count,
                                                const ClassScalars& k, const AdamWArgs& a,
                                                float (&p)[kVec], const float (&g)[kVec],
                                                float (&m)[kVec], float (&v)[kVec]) {
@@ -514,32 +528,36 @@ __global__ void __launch_bounds__(kThreads, SRS_ADAMW_MIN_CTAS)
     k.fast_math = a.fast_math[cls] != 0;
     k.m_floor = a.m_floor[cls];
     const int64_t end = row_end_tile(t, rv);
-    int64_t e0 = (t.tile - rv.tile_begin) * kTile + (int64_t)threadIdx.x * kVec;
     if constexpr (KIND != kKindMixed) {
-      if ((rv.flags & SRS_ROW_VECTOR_OK) != 0u && (rv.flags & 3u) == (uint32_t)KIND) {
-        // Tiles whose 2048 elements all lie inside the row.
+      if ((rv.flags & SRS_ROW_VECTOR_OK) != 0u && (rv.flags & 3u) == (uint32_t)KIND &&
+          rv.numel <= (int64_t)kMaxStagedRow) {
+        // Tiles whose 2048 elements all lie inside the row, addressed by a 32-bit
+        // element offset within the row.
         constexpr bool PB = (KIND & 1) != 0, GB = (KIND & 2) != 0;
         using S = Stage<PB ? 2 : 4, GB ? 2 : 4, MF, VF>;
         extern __shared__ __align__(16) char stage_mem[];
         const int64_t full_end = min(end, rv.tile_begin + rv.numel / kTile);
         const int n_full = t.tile < full_end ? (int)(full_end - t.tile) : 0;
+        uint32_t eo = (uint32_t)(t.tile - rv.tile_begin) * (uint32_t)kTile + threadIdx.x * kVec;
         for (int d = 0; d < kStages - 1; ++d) {
           if (d < n_full)
-            stage_issue<PB ? 2 : 4, GB ? 2 : 4, MF, VF>(rv, e0 + d * kTile, stage_mem + d * S::kBytes);
+            stage_issue<PB ? 2 : 4, GB ? 2 : 4, MF, VF>(rv, eo + d * (uint32_t)kTile,
+                                                        stage_mem + d * S::kBytes);
           cp_async_commit();
         }
-        for (int i = 0; i < n_full; ++i, e0 += kTile) {
+        for (int i = 0; i < n_full; ++i, eo += (uint32_t)kTile) {
           if (i + kStages - 1 < n_full)
             stage_issue<PB ? 2 : 4, GB ? 2 : 4, MF, VF>(
-                rv, e0 + (kStages - 1) * kTile,
+                rv, eo + (kStages - 1) * (uint32_t)kTile,
                 stage_mem + ((i + kStages - 1) % kStages) * S::kBytes);
           cp_async_commit();
           cp_async_wait_stage();
-          adamw8_staged<PB, GB, MF, VF>(rv, e0, k, a, stage_mem + (i % kStages) * S::kBytes);
+          adamw8_staged<PB, GB, MF, VF>(rv, (int64_t)eo, k, a, stage_mem + (i % kStages) * S::kBytes);
         }
         t.tile += n_full;
       }
     }
+    int64_t e0 = (t.tile - rv.tile_begin) * kTile + (int64_t)threadIdx.x * kVec;
     for (; t.tile < end; ++t.tile, e0 += kTile) {
       if (e0 < rv.numel) {
         const int count = (int)min((int64_t)kVec, rv.numel - e0);
@@ -555,8 +573,8 @@ __global__ void __launch_bounds__(kThreads, SRS_ADAMW_MIN_CTAS)
 // ----------------------------------------------------------------- SGDM --
 
 // u' = u*mf + g (two roundings); p' = fma(u', -lr, p)  (sr_states/reference/sgd.py:62-64).
-template <bool PB, int UF, bool VEC>
-__device__ __forceinline__ void sgdm8_compute(const RowView& rv, int64_t e0, int count,
+template <bool PB, int UF, bool VEC, typename I>
+__device__ __forceinline__ void sgdm8_compute(const RowView& rv, I e0, int count,
                                               const SgdmArgs& a, float (&p)[kVec],
                                               const float (&g)[kVec], float (&u)[kVec]) {
   const float2 mf = splat(a.hp.momentum), nlr = splat(a.hp.neg_lr);
@@ -585,7 +603,7 @@ __device__ __forceinline__ void sgdm8(const RowView& rv, int64_t e0, int count,
 }
 
 template <bool PB, bool GB, int UF>
-__device__ __forceinline__ void sgdm8_staged(const RowView& rv, int64_t e0, const SgdmArgs& a,
+__device__ __forceinline__ void sgdm8_staged(const RowView& rv, uint32_t e0, const SgdmArgs& a,
                                              const char* stage) {
   constexpr int PBYTES = PB ? 2 : 4, GBYTES = GB ? 2 : 4;
   constexpr int PF = PB ? SRS_FMT_BF16 : SRS_FMT_F32, GF = GB ? SRS_FMT_BF16 : SRS_FMT_F32;
@@ -626,31 +644,34 @@ __global__ void __launch_bounds__(kThreads)
   do {
     const RowView rv = make_view(rows != nullptr ? load_row(rows + t.r) : a.inline_row, a);
     const int64_t end = row_end_tile(t, rv);
-    int64_t e0 = (t.tile - rv.tile_begin) * kTile + (int64_t)threadIdx.x * kVec;
     if constexpr (KIND != kKindMixed) {
-      if ((rv.flags & SRS_ROW_VECTOR_OK) != 0u && (rv.flags & 3u) == (uint32_t)KIND) {
+      if ((rv.flags & SRS_ROW_VECTOR_OK) != 0u && (rv.flags & 3u) == (uint32_t)KIND &&
+          rv.numel <= (int64_t)kMaxStagedRow) {
         constexpr bool PB = (KIND & 1) != 0, GB = (KIND & 2) != 0;
         using S = Stage<PB ? 2 : 4, GB ? 2 : 4, UF, -1>;
         extern __shared__ __align__(16) char stage_mem[];
         const int64_t full_end = min(end, rv.tile_begin + rv.numel / kTile);
         const int n_full = t.tile < full_end ? (int)(full_end - t.tile) : 0;
+        uint32_t eo = (uint32_t)(t.tile - rv.tile_begin) * (uint32_t)kTile + threadIdx.x * kVec;
         for (int d = 0; d < kStages - 1; ++d) {
           if (d < n_full)
-            stage_issue<PB ? 2 : 4, GB ? 2 : 4, UF, -1>(rv, e0 + d * kTile, stage_mem + d * S::kBytes);
+            stage_issue<PB ? 2 : 4, GB ? 2 : 4, UF, -1>(rv, eo + d * (uint32_t)kTile,
+                                                        stage_mem + d * S::kBytes);
           cp_async_commit();
         }
-        for (int i = 0; i < n_full; ++i, e0 += kTile) {
+        for (int i = 0; i < n_full; ++i, eo += (uint32_t)kTile) {
           if (i + kStages - 1 < n_full)
             stage_issue<PB ? 2 : 4, GB ? 2 : 4, UF, -1>(
-                rv, e0 + (kStages - 1) * kTile,
+                rv, eo + (kStages - 1) * (uint32_t)kTile,
                 stage_mem + ((i + kStages - 1) % kStages) * S::kBytes);
           cp_async_commit();
           cp_async_wait_stage();
-          sgdm8_staged<PB, GB, UF>(rv, e0, a, stage_mem + (i % kStages) * S::kBytes);
+          sgdm8_staged<PB, GB, UF>(rv, eo, a, stage_mem + (i % kStages) * S::kBytes);
         }
         t.tile += n_full;
       }
     }
+    int64_t e0 = (t.tile - rv.tile_begin) * kTile + (int64_t)threadIdx.x * kVec;
     for (; t.tile < end; ++t.tile, e0 += kTile) {
       if (e0 < rv.numel) {
         const int count = (int)min((int64_t)kVec, rv.numel - e0);

@@ -15,6 +15,7 @@ a single launch per device instead of one per bucket.
 
 from __future__ import annotations
 
+import collections
 from dataclasses import dataclass
 
 import numpy as np
@@ -37,21 +38,32 @@ class Update:
     step: int | None
 
 
+def _positive_step(step, uses_step):
+    """The AdamW bias-correction step of an item (None for optimizers without one)."""
+    if not uses_step:
+        return None
+    if isinstance(step, bool) or not isinstance(step, int) or step < 1:
+        raise ValueError("step must be a positive integer")
+    return step
+
+
 def collect_updates(items, state_names, *, uses_step):
-    """Validate every item and group the non-empty ones by device (order kept)."""
-    by_device: dict[torch.device, list[Update]] = {}
+    """{device: [Update, ...]} of a group's items, in item order.
+
+    The tensors of every item are validated on every full preparation: the
+    row-table cache keys on addresses, and an in-place resize or restride keeps
+    those.  Empty parameters are validated too but add no row (their device
+    still gets an entry, so its capability is checked)."""
+    per_device = collections.defaultdict(list)
     for parameter, state, param_index, step, offset in items:
-        tensors = (parameter, parameter.grad, *(state[name] for name in state_names))
-        # A resize or restride can keep data_ptr unchanged: check the layout every time.
+        tensors = (parameter, parameter.grad) + tuple(state[name] for name in state_names)
         check_layout(tensors)
-        if uses_step and (not isinstance(step, int) or isinstance(step, bool) or step < 1):
-            raise ValueError("step must be a positive integer")
-        rows = by_device.setdefault(parameter.device, [])
-        numel = parameter.numel()
-        if numel:
-            rows.append(Update(tensors, int(param_index), numel, int(offset) & _MASK32,
-                               step if uses_step else None))
-    return by_device
+        update = Update(tensors, int(param_index), parameter.numel(), int(offset) & _MASK32,
+                        _positive_step(step, uses_step))
+        rows = per_device[parameter.device]
+        if update.numel > 0:
+            rows.append(update)
+    return dict(per_device)
 
 
 @dataclass

@@ -36,9 +36,10 @@ Checkpoints: ``state_dict()`` gathers the shards into the unsharded layout of
 AdamWReferenceSR / SGDMReferenceSR (every state in its parameter's shape), so
 a checkpoint resumes at any world size or in the unsharded optimizer, and
 ``load_state_dict`` accepts that layout and keeps the local runs.  Both are
-collectives.  ``sharded_state_dict()`` / ``load_sharded_state_dict()`` save and
-restore each rank's own runs without communication (same world size and
-parameters required).
+collectives; ``state_dict(to_rank=r)`` delivers the runs to rank r only (a
+gather, in bounded buckets).  ``sharded_state_dict()`` /
+``load_sharded_state_dict()`` save and restore each rank's own runs without
+communication (same world size and parameters required).
 """
 
 from __future__ import annotations
@@ -118,16 +119,21 @@ class FlatLayout:
             storage, 0, (padded,), (1,))
         return base
 
-    def shard(self, dtype) -> tuple[int, int]:
+    def shard(self, dtype, rank=None) -> tuple[int, int]:
         size = self.buffers[dtype].numel() // self.world
-        return self.rank * size, (self.rank + 1) * size
+        rank = self.rank if rank is None else rank
+        return rank * size, (rank + 1) * size
+
+    def run_on(self, p, rank) -> tuple[int, int] | None:
+        """[lo, hi) of p's flattened elements that ``rank`` updates, or None."""
+        dtype, offset = self.place[id(p)]
+        start, stop = self.shard(dtype, rank)
+        lo, hi = max(start, offset) - offset, min(stop, offset + p.numel()) - offset
+        return (lo, hi) if lo < hi else None
 
     def local_run(self, p) -> tuple[int, int] | None:
         """[lo, hi) of p's flattened elements that this rank updates, or None."""
-        dtype, offset = self.place[id(p)]
-        start, stop = self.shard(dtype)
-        lo, hi = max(start, offset) - offset, min(stop, offset + p.numel()) - offset
-        return (lo, hi) if lo < hi else None
+        return self.run_on(p, self.rank)
 
 
 def peer_order(rank: int, world: int) -> list[int]:
@@ -446,7 +452,7 @@ class _ZeroMixin:
         for dtype, buffer in self._grad_buffers.items():
             lo, hi = self._layout.shard(dtype)
             if gloo:  # gloo has no reduce-scatter of a flat tensor: reduce everything
-                dist.all_reduce(buffer, group=self._group)
+                self._collective(dist.all_reduce, buffer)
             else:
                 dist.reduce_scatter_tensor(buffer[lo:hi], buffer, group=self._group)
             if op == "mean":
@@ -457,53 +463,125 @@ class _ZeroMixin:
     def _ordered_params(self):
         return [p for g in self.param_groups for p in g["params"]]
 
-    def state_dict(self):
-        """The unsharded state dict (the layout of the unsharded optimizer),
-        assembled from every rank's runs.  A collective: call it on every rank."""
+    def state_dict(self, *, to_rank: int | None = None, bucket_bytes: int = 1 << 28):
+        """The unsharded state dict: every state in its parameter's shape, the
+        layout of the unsharded optimizer, so it resumes at any world size or
+        in that optimizer.  A collective: call it on every rank.
+
+        Each rank contributes only its runs.  ``to_rank=None``: every rank
+        receives the others' runs (an all-gather) and returns the whole dict;
+        ``to_rank=r``: only rank r receives them (a gather) and returns the
+        dict, the other ranks return ``{}``.  The runs travel in buckets of
+        about ``bucket_bytes`` of states, so the transient memory beyond the
+        result stays bounded."""
         local = super().state_dict()
+        if self._world > 1 and to_rank is not None and not 0 <= to_rank < self._world:
+            raise ValueError(f"to_rank must be a rank of the group, got {to_rank}")
+        receive = to_rank is None or to_rank == self._rank
         params = self._ordered_params()
-        if self._world == 1 and not any(
-                n in st for st in self.state.values() for n in self._state_names):
-            return local
+        names = self._state_names
+        formats = self.param_formats()
         device = next(iter(self._layout.buffers.values())).device
-        # Which parameters have states anywhere, and their steps.
+        # Which parameters have states on any rank, and their AdamW steps.
         present = torch.zeros(len(params), dtype=torch.int64, device=device)
         steps = torch.zeros(len(params), dtype=torch.int64, device=device)
         for i, p in enumerate(params):
             st = self.state.get(p, {})
-            if self._state_names[0] in st:
+            if any(n in st for n in names):
                 present[i] = 1
                 steps[i] = int(st.get("step", 0))
         if self._world > 1:
-            torch.distributed.all_reduce(present, op=torch.distributed.ReduceOp.MAX,
-                                         group=self._group)
-            torch.distributed.all_reduce(steps, op=torch.distributed.ReduceOp.MAX,
-                                         group=self._group)
+            for flags in (present, steps):
+                self._collective(torch.distributed.all_reduce, flags,
+                                 op=torch.distributed.ReduceOp.MAX)
+        present, steps = present.tolist(), steps.tolist()
+        wanted = [(i, name, fmt) for i, p in enumerate(params) if present[i]
+                  for name, fmt in zip(names, formats[id(p)])]
+        full = {}
+        for bucket in _buckets(wanted, params, bucket_bytes):
+            full.update(self._gather_runs(bucket, params, to_rank, receive, device))
+        if not receive:
+            return {}
         state = {}
         for i, p in enumerate(params):
             if not present[i]:
                 continue
-            run = self._layout.local_run(p)
-            st = self.state.get(p, {})
-            entry = {}
-            for group in self.param_groups:
-                if any(q is p for q in group["params"]):
-                    formats = self._formats(group)
-                    break
-            for name, fmt in zip(self._state_names, formats):
-                full = torch.zeros(p.numel(), dtype=fmt.dtype, device=p.device)
-                if run is not None and name in st:
-                    full[run[0]:run[1]].copy_(st[name])
-                if self._world > 1:
-                    # Each element is non-zero on at most one rank: summing the
-                    # bytes assembles the state exactly, whatever its dtype.
-                    torch.distributed.all_reduce(full.view(torch.uint8), group=self._group)
-                entry[name] = full.view(p.shape)
+            entry = {name: full[i, name].view(p.shape) for name in names}
             if self._uses_step:
                 entry["step"] = int(steps[i])
             state[i] = entry
         local["state"] = state
         return local
+
+    def _collective(self, fn, tensor, *args, **kwargs):
+        """Run a collective on ``tensor``; with gloo, device tensors go through
+        host memory (gloo moves host buffers)."""
+        dist = torch.distributed
+        if tensor.device.type == "cuda" and dist.get_backend(self._group) == "gloo":
+            host = tensor.cpu()
+            fn(host, *args, group=self._group, **kwargs)
+            tensor.copy_(host)
+        else:
+            fn(tensor, *args, group=self._group, **kwargs)
+
+    def _gather_runs(self, bucket, params, to_rank, receive, device):
+        """{(param index, state name): full-size state} of one bucket, assembled
+        from every rank's runs (on the receiving ranks; {} elsewhere)."""
+        layout, world = self._layout, self._world
+
+        def runs(rank):
+            out = []
+            for i, name, fmt in bucket:
+                run = layout.run_on(params[i], rank)
+                if run is not None:
+                    out.append((i, name, fmt, run))
+            return out
+
+        def nbytes(rank):
+            return sum((hi - lo) * _itemsize(fmt.dtype) for _, _, fmt, (lo, hi) in runs(rank))
+
+        width = max(nbytes(r) for r in range(world))
+        mine = torch.zeros(width, dtype=torch.uint8, device=device)
+        at = 0
+        for i, name, fmt, (lo, hi) in runs(self._rank):
+            size = (hi - lo) * _itemsize(fmt.dtype)
+            held = self.state.get(params[i], {}).get(name)
+            if held is not None:
+                mine[at:at + size].copy_(held.reshape(-1).view(torch.uint8))
+            at += size
+        if world == 1:
+            everyone = [mine]
+        else:
+            everyone = self._exchange(mine, to_rank, receive)
+        if not receive:
+            return {}
+        full = {(i, name): torch.zeros(params[i].numel(), dtype=fmt.dtype, device=device)
+                for i, name, fmt in bucket}
+        for rank, chunk in enumerate(everyone):
+            at = 0
+            for i, name, fmt, (lo, hi) in runs(rank):
+                size = (hi - lo) * _itemsize(fmt.dtype)
+                full[i, name][lo:hi].view(torch.uint8).copy_(chunk[at:at + size])
+                at += size
+        return full
+
+    def _exchange(self, mine, to_rank, receive):
+        """Every rank's equally sized byte buffer: [rank 0's, rank 1's, ...] on the
+        receiving ranks (None elsewhere)."""
+        dist, world = torch.distributed, self._world
+        gloo = dist.get_backend(self._group) == "gloo"
+        send = mine.cpu() if gloo and mine.is_cuda else mine
+        if to_rank is None:
+            out = torch.empty(world * send.numel(), dtype=torch.uint8, device=send.device)
+            dist.all_gather_into_tensor(out, send, group=self._group)
+            chunks = list(out.view(world, -1))
+        else:
+            dst = dist.get_global_rank(self._group, to_rank) if self._group is not None else to_rank
+            chunks = [torch.empty_like(send) for _ in range(world)] if receive else None
+            dist.gather(send, chunks, dst=dst, group=self._group)
+        if not receive:
+            return None
+        return [c.to(mine.device) for c in chunks]
 
     def load_state_dict(self, state_dict):
         """Load the unsharded layout (from ``state_dict()`` here or from the
@@ -598,7 +676,14 @@ class _ZeroMixin:
         elif self._world > 1:
             for dtype, buffer in self._layout.buffers.items():
                 lo, hi = self._layout.shard(dtype)
-                torch.distributed.all_gather_into_tensor(buffer, buffer[lo:hi], group=self._group)
+                if buffer.is_cuda and torch.distributed.get_backend(self._group) == "gloo":
+                    host = buffer.cpu()  # gloo moves host buffers
+                    torch.distributed.all_gather_into_tensor(host, host[lo:hi].clone(),
+                                                             group=self._group)
+                    buffer.copy_(host)
+                else:
+                    torch.distributed.all_gather_into_tensor(buffer, buffer[lo:hi],
+                                                             group=self._group)
         if marks:
             marks[3].record(stream)
             self._events.append(marks)
@@ -736,6 +821,26 @@ class ZeroAdamW(_ZeroMixin, AdamWReferenceSR):
 
 class ZeroSGDM(_ZeroMixin, SGDMReferenceSR):
     """Momentum SGD (fused, sm_100a) with ZeRO-1 sharded states."""
+
+
+def _itemsize(dtype) -> int:
+    return torch.empty((), dtype=dtype).element_size()
+
+
+def _buckets(wanted, params, limit):
+    """Split [(param index, state name, format), ...] into lists of about
+    ``limit`` bytes of full-size states each (at least one entry per list)."""
+    bucket, size = [], 0
+    for item in wanted:
+        i, _, fmt = item
+        nbytes = params[i].numel() * _itemsize(fmt.dtype)
+        if bucket and size + nbytes > limit:
+            yield bucket
+            bucket, size = [], 0
+        bucket.append(item)
+        size += nbytes
+    if bucket:
+        yield bucket
 
 
 def shard_sizes(numel_total: int, world: int) -> int:

@@ -141,6 +141,18 @@ def _checkpoint_worker(rank, world, port, queue):
         sharded = _run(ZeroAdamW, params, grads[:2], fmt)
         full = sharded.state_dict()
         expected = ref_opt.state_dict()
+        # Gathered to one rank, in many small buckets: the same dict there, {} elsewhere.
+        last = world - 1
+        one = sharded.state_dict(to_rank=last, bucket_bytes=64)
+        if rank == last:
+            assert set(one["state"]) == set(full["state"]) and one["param_groups"] == full["param_groups"]
+            for key, entry in full["state"].items():
+                assert one["state"][key].keys() == entry.keys()
+                for name in ("exp_avg", "exp_avg_sq"):
+                    assert torch.equal(one["state"][key][name].view(torch.uint8),
+                                       entry[name].view(torch.uint8))
+        else:
+            assert one == {}
         assert set(full["state"]) == set(expected["state"])
         for key, entry in expected["state"].items():
             mine = full["state"][key]
