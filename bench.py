@@ -28,6 +28,10 @@ Other workloads of the same path (one GPU; not the headline):
     --workload adamw-70b   AdamW at the Llama-3-70B shape with FP16 stochastic
                            states on 4 or 8 GPUs, everything sharded (see
                            run_adamw_70b)
+    --workload nvlink-exchange
+                           the fused step's peer stores in isolation: one
+                           process, GPU 0 updating and storing into a replica
+                           on GPU 1 (for NVLink counters; needs two GPUs)
 """
 
 from __future__ import annotations
@@ -78,9 +82,13 @@ def parse_args(argv=None):
     parser.add_argument("--no-embeddings", action="store_true",
                         help="drop the two 128256x4096 matrices (profiling case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast", "adamw-70b"),
+    parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast", "adamw-70b",
+                                               "nvlink-exchange"),
                         default="adamw-8b")
-    parser.add_argument("--gather", choices=("auto", "fused", "copy", "nccl"), default="auto",
+    parser.add_argument("--exchange-elems", type=int, default=1 << 26,
+                        help="parameters of the nvlink-exchange workload")
+    parser.add_argument("--gather", choices=("auto", "fused", "copy", "nccl", "multicast"),
+                        default="auto",
                         help="how the sharded step reassembles the parameters at N>1")
     parser.add_argument("--chunks", type=int, default=32,
                         help="tile chunks of the pipelined exchange (--gather copy)")
@@ -620,6 +628,9 @@ def run_b200(args):
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",
                    "gather": {"fused": "updated parameters stored into every peer replica by "
                                        "the step kernel (NVLink peer stores)",
+                              "multicast": "each updated vector stored once by the step kernel "
+                                           "to an NVLink multicast address (multimem.st); "
+                                           "NVSwitch delivers it to every replica",
                               "copy": "copy engines send each chunk of updated parameters to "
                                       "the peers while the next chunk is updated",
                               "nccl": "NCCL all-gather after the step",
@@ -903,6 +914,75 @@ def run_adamw_70b(args):
     dist.destroy_process_group()
 
 
+def run_nvlink_exchange(args):
+    """The fused exchange of a sharded AdamW step in isolation, in ONE process
+    driving two GPUs: GPU 0 updates --exchange-elems parameters (config-4
+    formats) and stores every updated BF16 vector both locally and into a
+    replica on GPU 1 over NVLink (peer stores from the step kernel, as ZeRO-1's
+    fused gather does at N=2).  One process, so a profiler can capture the
+    kernel's NVLink counters on GPU 0 alone.  Prints the kernel time, the
+    NVLink bytes it must send and the rate, and checks the replica."""
+    import torch
+    from cuda.bindings import runtime as cudart
+
+    from sr_states.cuda import _native
+    from sr_states.cuda._fused import adamw_hparams, rng_words
+    from sr_states.cuda._tables import DeviceTable, Update, build_table, upload
+
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("--workload nvlink-exchange needs two GPUs in one process")
+    src, dst = torch.device("cuda", 0), torch.device("cuda", 1)
+    torch.cuda.set_device(src)
+    err, = cudart.cudaSetDevice(0)[:1]
+    err2, = cudart.cudaDeviceEnablePeerAccess(1, 0)[:1]
+    if int(err) != 0 or int(err2) not in (0, int(cudart.cudaError_t.cudaErrorPeerAccessAlreadyEnabled)):
+        raise SystemExit(f"peer access 0 -> 1 unavailable ({err}, {err2})")
+    n = args.exchange_elems
+    gen = torch.Generator(device=src).manual_seed(SEED)
+    p = torch.empty(n, dtype=torch.bfloat16, device=src).normal_(0, 0.02, generator=gen)
+    g = torch.empty(n, dtype=torch.bfloat16, device=src).normal_(0, 1e-4, generator=gen)
+    m = torch.zeros(n, dtype=torch.float8_e4m3fn, device=src)
+    v = torch.zeros(n, dtype=torch.bfloat16, device=src)
+    replica = torch.zeros(n, dtype=torch.bfloat16, device=dst)
+    host = build_table([Update((p, g, m, v), 0, n, 0, 1)], [0], 2048)
+    n_tiles = int(-(-n // 2048))
+    table = DeviceTable(host, upload(host, src), 1, n_tiles)
+    peers = _native.SrsPeers()
+    peers.n_peers = 1
+    peers.delta_bf16[0] = replica.data_ptr() - p.data_ptr()
+    launcher = _native.launcher()
+    launcher.check_device(src)
+    stream = torch.cuda.current_stream(src)
+
+    def launch(i):
+        hp = adamw_hparams(LR, BETAS, EPS, WEIGHT_DECAY, (i + 1,))
+        launcher.adamw_multi(table, 1, n_tiles, 3, 1, 1, 1, hp, rng_words(SEED, i + 1),
+                             stream.cuda_stream, peers=peers)
+
+    for i in range(args.warmup):
+        launch(i)
+    torch.cuda.synchronize(src)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.warmup, args.warmup + args.steps):
+        launch(i)
+    end.record(stream)
+    torch.cuda.synchronize(src)
+    torch.cuda.synchronize(dst)
+    ms = start.elapsed_time(end) / args.steps
+    same = bool(torch.equal(replica.view(torch.int16).cpu(), p.view(torch.int16).cpu()))
+    print(json.dumps({
+        "metric": "fused AdamW step + peer stores, one GPU to one peer over NVLink",
+        "value": 2 * n / (ms / 1e3) / 1e9, "unit": "GB/s NVLink (BF16 bytes stored to the peer)",
+        "n_gpus": 2, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "data": "synthetic",
+        "config": {"workload": "nvlink-exchange", "elements": n, "formats": "BF16 p/g, E4M3 SR "
+                   "m, BF16 SR v", "hbm_bytes_per_launch": BYTES_PER_PARAM * n,
+                   "nvlink_bytes_per_launch": 2 * n},
+        "hbm_gbs": BYTES_PER_PARAM * n / (ms / 1e3) / 1e9, "replica_equal": same,
+        "gpu_launches": args.steps}), flush=True)
+
+
 def run_reference(args):
     """The reference arm: the reference's own CPU implementation of the step
     (``AdamWReferenceSR.step`` of the unmodified package in baseline/_ref) on
@@ -948,6 +1028,8 @@ def main(argv=None):
         run_cast(args)
     elif args.workload == "adamw-70b":
         run_adamw_70b(args)
+    elif args.workload == "nvlink-exchange":
+        run_nvlink_exchange(args)
     else:
         run_b200(args)
 

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define SRS_ABI_VERSION 5
+#define SRS_ABI_VERSION 6
 
 /* ---- status codes ------------------------------------------------------ */
 #define SRS_OK 0
@@ -169,11 +169,30 @@ int srs_sgdm_multi(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int u_f
  * still reads its replica, and one after, before anyone uses the result).
  */
 #define SRS_MAX_PEERS 7
+/* How the updated parameters reach the replicas (srs_peers.mode):
+ *   SRS_PEERS_STORE      each vector is stored locally and at delta_*[w] for
+ *                        every peer w (plain stores through peer mappings);
+ *   SRS_PEERS_MULTICAST  the caller's flat buffers are bound to an NVLink
+ *                        multicast object spanning every rank (this one
+ *                        included) and mc_delta_* = (multicast address of the
+ *                        buffer) - (this rank's buffer): each aligned 8-element
+ *                        vector is written ONCE, with multimem.st, and NVSwitch
+ *                        delivers it to every replica, the local one included.
+ *                        Elements outside aligned vectors (row tails, rows
+ *                        without SRS_ROW_VECTOR_OK), which multimem cannot
+ *                        store at 2-byte granularity, take the SRS_PEERS_STORE
+ *                        path, so delta_*[] must hold the peers as well.
+ * Both end with a system-scope fence (and a proxy fence for the multicast
+ * alias), so the caller's barrier after the step publishes every replica. */
+#define SRS_PEERS_STORE 0
+#define SRS_PEERS_MULTICAST 1
 typedef struct srs_peers {
   int32_t n_peers; /* 0..SRS_MAX_PEERS */
-  int32_t reserved;
+  int32_t mode;    /* SRS_PEERS_STORE or SRS_PEERS_MULTICAST */
   int64_t delta_f32[SRS_MAX_PEERS];
   int64_t delta_bf16[SRS_MAX_PEERS];
+  int64_t mc_delta_f32;  /* SRS_PEERS_MULTICAST: multicast address - local buffer */
+  int64_t mc_delta_bf16;
 } srs_peers;
 
 int srs_adamw_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int m_format,

@@ -271,6 +271,13 @@ static int check_peers(const srs_peers* peers) {
   if (peers->n_peers < 0 || peers->n_peers > SRS_MAX_PEERS)
     return fail(SRS_ERR_INVALID_ARGUMENT, "n_peers must be in [0, %d], got %d", SRS_MAX_PEERS,
                 peers->n_peers);
+  if (peers->mode != SRS_PEERS_STORE && peers->mode != SRS_PEERS_MULTICAST)
+    return fail(SRS_ERR_INVALID_ARGUMENT, "unknown peers mode %d", peers->mode);
+  if (peers->mode == SRS_PEERS_MULTICAST &&
+      ((peers->mc_delta_bf16 % 16) != 0 || (peers->mc_delta_f32 % 16) != 0))
+    return fail(SRS_ERR_INVALID_ARGUMENT,
+                "multicast deltas must keep 16-byte alignment (got %lld, %lld)",
+                (long long)peers->mc_delta_bf16, (long long)peers->mc_delta_f32);
   return SRS_OK;
 }
 

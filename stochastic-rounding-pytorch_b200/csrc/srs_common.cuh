@@ -607,9 +607,25 @@ __device__ __forceinline__ void load_param8(const void* base, I e0, int count, b
   }
 }
 
+// One 8-element vector written through an NVLink multicast address: every
+// replica bound to the multicast object receives it (16-byte multimem stores;
+// two for FP32).  The address must be 16-byte aligned.
+template <int F>
+__device__ __forceinline__ void multimem_store8(char* mc, const uint32_t (&w)[kWords<F>]) {
+#pragma unroll
+  for (int i = 0; i < kWords<F>; i += 4)
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+                 ::"l"(mc + 4 * i), "f"(__uint_as_float(w[i])), "f"(__uint_as_float(w[i + 1])),
+                   "f"(__uint_as_float(w[i + 2])), "f"(__uint_as_float(w[i + 3]))
+                 : "memory");
+}
+
 // Parameter write-back: FP32 as is, BF16 round-to-nearest-even.  With peers,
-// the same bytes also go to the same offset of every peer's replica (plain
-// stores through the peer mappings: the fused all-gather of a sharded step).
+// the same bytes also reach the same offset of every peer's replica (the fused
+// all-gather of a sharded step): plain stores through the peer mappings, or,
+// in multicast mode, one multimem store per aligned vector that NVSwitch
+// delivers to every replica, this one included (element-wise tails use the
+// plain stores, multimem having no 2-byte form).
 template <bool BF16, typename I>
 __device__ __forceinline__ void store_param8(void* base, I e0, int count, bool vec,
                                              const float (&x)[kVec],
@@ -617,6 +633,12 @@ __device__ __forceinline__ void store_param8(void* base, I e0, int count, bool v
   constexpr int F = BF16 ? SRS_FMT_BF16 : SRS_FMT_F32;
   uint32_t w[kWords<F>];
   encode8<F>(x, 0u, SRS_RULE_NEAREST, w);
+  if (vec && peers != nullptr && peers->mode == SRS_PEERS_MULTICAST) {
+    multimem_store8<F>(const_cast<char*>(elem_ptr<F>(base, e0)) +
+                           (BF16 ? peers->mc_delta_bf16 : peers->mc_delta_f32),
+                       w);
+    return;
+  }
   if (vec) store_raw8<F>(base, e0, w);
   else store_raw_partial<F>(base, e0, count, w);
   if (peers != nullptr) {

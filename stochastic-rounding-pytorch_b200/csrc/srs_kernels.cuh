@@ -247,6 +247,14 @@ __device__ __forceinline__ void stage_read(const char* stage, int block, uint32_
 
 __device__ __forceinline__ float2 splat(float x) { return make_float2(x, x); }
 
+// End of a step that wrote replicas: order the peer or multicast stores before
+// whatever the caller's closing barrier releases (a proxy fence first for
+// multicast, whose stores reach this GPU's buffer through another address).
+__device__ __forceinline__ void publish_replicas(const srs_peers& peers) {
+  if (peers.mode == SRS_PEERS_MULTICAST) asm volatile("fence.proxy.alias;" ::: "memory");
+  if (peers.n_peers > 0 || peers.mode == SRS_PEERS_MULTICAST) __threadfence_system();
+}
+
 // --------------------------------------------------------------- AdamW --
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -566,8 +574,7 @@ __global__ void __launch_bounds__(kThreads, SRS_ADAMW_MIN_CTAS)
       }
     }
   } while (next_row(t, n_rows));
-  // Peer stores become visible to the peers before the step's closing barrier.
-  if (a.peers.n_peers > 0) __threadfence_system();
+  publish_replicas(a.peers);
 }
 
 // ----------------------------------------------------------------- SGDM --
@@ -680,7 +687,7 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
   } while (next_row(t, n_rows));
-  if (a.peers.n_peers > 0) __threadfence_system();
+  publish_replicas(a.peers);
 }
 
 // ----------------------------------------------------------------- cast --

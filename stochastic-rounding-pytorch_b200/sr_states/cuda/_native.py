@@ -71,10 +71,14 @@ MAX_PEERS = 7
 IPC_HANDLE_BYTES = 64
 
 
+PEERS_STORE, PEERS_MULTICAST = 0, 1
+
+
 class SrsPeers(ctypes.Structure):
-    _fields_ = [("n_peers", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    _fields_ = [("n_peers", ctypes.c_int32), ("mode", ctypes.c_int32),
                 ("delta_f32", ctypes.c_int64 * MAX_PEERS),
-                ("delta_bf16", ctypes.c_int64 * MAX_PEERS)]
+                ("delta_bf16", ctypes.c_int64 * MAX_PEERS),
+                ("mc_delta_f32", ctypes.c_int64), ("mc_delta_bf16", ctypes.c_int64)]
 
 
 _P = ctypes.c_void_p
@@ -124,7 +128,7 @@ _SIGNATURES = {
     "srs_ipc_close": ([_P], ctypes.c_int),
 }
 NOALLOC_MAX_ROWS = 4096
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 _lock = threading.Lock()
 _library = None

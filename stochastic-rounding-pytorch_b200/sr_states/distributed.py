@@ -20,6 +20,10 @@ is then: barrier (no peer still reads its replica), fused launch, barrier
 current stream.  If any rank cannot export its buffers (for example memory
 from the virtual-memory allocator), all ranks fall back to one in-place NCCL
 all-gather per flat buffer after the update (``gather="nccl"`` selects it).
+``gather="multicast"`` allocates the flat buffers from PyTorch's symmetric
+memory and binds them to an NVLink multicast object: the kernel then writes
+each updated vector once (``multimem.st``) and NVSwitch delivers it to every
+replica; without multicast support it falls back to the peer stores.
 ``gather="copy"`` instead runs the step over ``chunks`` tile ranges and lets
 the copy engines send each finished range to the peers while the next one is
 updated.  The default, ``"auto"``, takes ``"copy"`` with one peer and
@@ -72,7 +76,10 @@ class _Piece:
 class FlatLayout:
     """Where every parameter lives in its dtype's flat buffer and which run is local."""
 
-    def __init__(self, params, world: int, rank: int):
+    def __init__(self, params, world: int, rank: int, allocate=None):
+        """``allocate(numel, dtype, device)`` makes the flat buffers (zeroed);
+        without it they are ordinary allocations, or the parameters' own
+        storage when that already holds exactly the layout."""
         self.world, self.rank = world, rank
         self.buffers: dict[torch.dtype, torch.Tensor] = {}
         self.place: dict[int, tuple[torch.dtype, int]] = {}  # id(param) -> (dtype, flat offset)
@@ -84,9 +91,10 @@ class FlatLayout:
             total = sum(p.numel() for p in plist)
             self.numel[dtype] = total
             padded = shard_sizes(total, world) * world
-            buffer = self._adopt(plist, padded)
+            buffer = None if allocate is not None else self._adopt(plist, padded)
             if buffer is None:
-                buffer = torch.zeros(padded, dtype=dtype, device=plist[0].device)
+                buffer = (allocate(padded, dtype, plist[0].device) if allocate is not None
+                          else torch.zeros(padded, dtype=dtype, device=plist[0].device))
                 offset = 0
                 for p in plist:
                     n = p.numel()
@@ -279,8 +287,9 @@ class _ZeroMixin:
 
     def __init__(self, params, *args, process_group=None, gather="auto", chunks=32,
                  grads="full", record_timings=False, **kwargs):
-        if gather not in ("auto", "fused", "copy", "nccl"):
-            raise ValueError(f"gather must be 'auto', 'fused', 'copy' or 'nccl', got {gather!r}")
+        if gather not in ("auto", "fused", "copy", "nccl", "multicast"):
+            raise ValueError("gather must be 'auto', 'fused', 'copy', 'nccl' or 'multicast', "
+                             f"got {gather!r}")
         if grads not in ("full", "reduce_scatter"):
             raise ValueError(f"grads must be 'full' or 'reduce_scatter', got {grads!r}")
         super().__init__(params, *args, **kwargs)
@@ -289,7 +298,13 @@ class _ZeroMixin:
         self._world = torch.distributed.get_world_size(process_group) if initialized else 1
         self._rank = torch.distributed.get_rank(process_group) if initialized else 0
         ordered = [p for g in self.param_groups for p in g["params"]]
-        self._layout = FlatLayout(ordered, self._world, self._rank)
+        symmetric = (gather == "multicast" and self._world > 1
+                     and all(p.device.type == "cuda" for p in ordered))
+        if gather == "multicast" and not symmetric:
+            gather = "auto"  # one rank or host tensors: no multicast to bind
+        self._layout = FlatLayout(ordered, self._world, self._rank,
+                                  allocate=_symmetric_zeros if symmetric else None)
+        self._symm_handles: dict = {}
         # CUDA events of the last steps (record_timings=True); bounded, so a run
         # that never reads `timings` keeps at most this many steps' events.
         self._record_timings = bool(record_timings)
@@ -315,9 +330,12 @@ class _ZeroMixin:
                 # beat the kernel's own peer stores (12.1 vs 13.4 ms per step); with
                 # three, concurrent peer copies fell to ~400 GB/s (33.6 vs 18.4 ms).
                 gather = "copy" if self._world == 2 else "fused"
-            if gather in ("fused", "copy"):
+            multicast = self._connect_multicast() if gather == "multicast" else None
+            if multicast is not None:
+                self._srs_peers = multicast
+            elif gather in ("fused", "copy", "multicast"):
                 connected = self._connect_peers()
-                if connected is not None and gather == "fused":
+                if connected is not None and gather in ("fused", "multicast"):
                     self._srs_peers = connected[0]
                 elif connected is not None:
                     self._srs_exchange = _ChunkedExchange(self._layout, connected[1], device,
@@ -325,7 +343,8 @@ class _ZeroMixin:
         if self._world == 1:
             self._gather = "none"
         elif self._srs_peers is not None:
-            self._gather = "fused"
+            self._gather = ("multicast" if self._srs_peers.mode == _peers_multicast()
+                            else "fused")
         else:
             self._gather = "copy" if self._srs_exchange is not None else "nccl"
         self._connected_gather = self._gather
@@ -333,8 +352,10 @@ class _ZeroMixin:
 
     @property
     def gather_mode(self) -> str:
-        """'fused' (peer stores inside the step), 'copy' (copy engines pipelined
-        with the step), 'nccl' (all-gather after it) or 'none' (one rank)."""
+        """'fused' (peer stores inside the step), 'multicast' (one NVLink
+        multicast store per vector inside the step), 'copy' (copy engines
+        pipelined with the step), 'nccl' (all-gather after it) or 'none' (one
+        rank)."""
         return self._gather
 
     def set_gather_mode(self, mode: str) -> None:
@@ -397,6 +418,49 @@ class _ZeroMixin:
             self._close_peers()
             return None
         return peers, starts
+
+    def _connect_multicast(self):
+        """Bind every rank's flat buffers (symmetric allocations) to NVLink
+        multicast objects: SrsPeers in multicast mode, with the peers' own
+        addresses for the element-wise tails; None on every rank if any rank
+        lacks multicast support (then peer stores are tried)."""
+        from .cuda import _native
+
+        group = self._group if self._group is not None else torch.distributed.group.WORLD
+        handles, mapped, multicast = {}, False, False
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            for dtype, buffer in self._layout.buffers.items():
+                handles[dtype] = symm_mem.rendezvous(buffer, group)
+            mapped = all(len(h.buffer_ptrs) == self._world for h in handles.values())
+            multicast = mapped and all(h.multicast_ptr != 0 for h in handles.values())
+        except (RuntimeError, ValueError, AttributeError, ImportError):
+            mapped = multicast = False
+        everyone = self._agree((mapped, multicast))
+        if not all(m for m, _ in everyone):
+            return None
+        peers = _native.SrsPeers()
+        # Without multicast support on every rank: plain peer stores through the
+        # symmetric mappings.
+        peers.mode = (_native.PEERS_MULTICAST if all(mc for _, mc in everyone)
+                      else _native.PEERS_STORE)
+        peers.n_peers = self._world - 1
+        for dtype, buffer in self._layout.buffers.items():
+            h = handles[dtype]
+            offset = buffer.data_ptr() - int(h.buffer_ptrs[self._rank])
+            mc = int(h.multicast_ptr) + offset - buffer.data_ptr() if h.multicast_ptr else 0
+            deltas = peers.delta_bf16 if dtype == torch.bfloat16 else peers.delta_f32
+            for n, r in enumerate(peer_order(self._rank, self._world)):
+                deltas[n] = int(h.buffer_ptrs[r]) + offset - buffer.data_ptr()
+            if peers.mode != _native.PEERS_MULTICAST:
+                continue
+            if dtype == torch.bfloat16:
+                peers.mc_delta_bf16 = mc
+            else:
+                peers.mc_delta_f32 = mc
+        self._symm_handles = handles
+        return peers
 
     def _close_peers(self):
         if self._peer_bases:
@@ -659,7 +723,7 @@ class _ZeroMixin:
         stream = (torch.cuda.current_stream()
                   if self._record_timings and torch.cuda.is_available() else None)
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if stream else None
-        fused = self._gather in ("fused", "copy")
+        fused = self._gather in ("fused", "copy", "multicast")
         if marks:
             marks[0].record(stream)
         if fused:
@@ -793,14 +857,19 @@ class _ZeroMixin:
         step, on every rank, while the process group still exists)."""
         self._events.clear()
         self._timed = []
-        if self._srs_exchange is not None:
+        if self._srs_exchange is not None or self._symm_handles:
+            torch.cuda.current_stream().synchronize()
+        if self._symm_handles and self._gather == "multicast":
+            self._barrier()  # no rank still stores through the multicast objects
             torch.cuda.current_stream().synchronize()
         self._close_peers()
         self._srs_peers = None
         self._srs_exchange = None
         self._host_pipeline = None
-        if self._gather in ("fused", "copy"):
+        if self._gather in ("fused", "copy", "multicast"):
             self._gather = "nccl"  # a later step all-gathers
+        # The multicast bindings (self._symm_handles) stay: the parameters live in
+        # those buffers.  They are released with the buffers, normally at exit.
         self._connected_gather = self._gather if self._world > 1 else "none"
         self._connected = (None, None)
 
@@ -821,6 +890,20 @@ class ZeroAdamW(_ZeroMixin, AdamWReferenceSR):
 
 class ZeroSGDM(_ZeroMixin, SGDMReferenceSR):
     """Momentum SGD (fused, sm_100a) with ZeRO-1 sharded states."""
+
+
+def _symmetric_zeros(numel, dtype, device):
+    """A zeroed flat buffer from PyTorch's symmetric-memory allocator (each rank's
+    buffer mappable by the others and bindable to an NVLink multicast object)."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    return symm_mem.empty(numel, dtype=dtype, device=device).zero_()
+
+
+def _peers_multicast() -> int:
+    from .cuda import _native
+
+    return _native.PEERS_MULTICAST
 
 
 def _itemsize(dtype) -> int:

@@ -39,6 +39,8 @@ def test_header_constants_match_python():
     assert int(define["SRS_ROW_GRAD_BF16"], 16) == _native.ROW_GRAD_BF16
     assert int(define["SRS_ROW_VECTOR_OK"], 16) == _native.ROW_VECTOR_OK
     assert int(define["SRS_ERR_INVALID_ARGUMENT"]) == _native.SRS_ERR_INVALID_ARGUMENT
+    assert int(define["SRS_PEERS_STORE"]) == _native.PEERS_STORE
+    assert int(define["SRS_PEERS_MULTICAST"]) == _native.PEERS_MULTICAST
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="needs a C compiler")
@@ -53,13 +55,18 @@ int main(void) {{
          sizeof(srs_sgdm_hparams));
   printf("%zu %zu %zu %zu\\n", offsetof(srs_row, numel), offsetof(srs_row, param_index),
          offsetof(srs_row, flags), offsetof(srs_adamw_hparams, neg_step_size));
+  printf("%zu %zu %zu %zu\\n", sizeof(srs_peers), offsetof(srs_peers, mode),
+         offsetof(srs_peers, delta_bf16), offsetof(srs_peers, mc_delta_bf16));
   return 0;
 }}
 """)
     exe = tmp_path / "layout"
     subprocess.run(["gcc", str(probe), "-o", str(exe)], check=True)
-    sizes, offsets = subprocess.run([str(exe)], capture_output=True, text=True,
-                                    check=True).stdout.split("\n")[:2]
+    sizes, offsets, peers = subprocess.run([str(exe)], capture_output=True, text=True,
+                                           check=True).stdout.split("\n")[:3]
+    assert [int(x) for x in peers.split()] == [
+        ctypes.sizeof(_native.SrsPeers), _native.SrsPeers.mode.offset,
+        _native.SrsPeers.delta_bf16.offset, _native.SrsPeers.mc_delta_bf16.offset]
     assert [int(x) for x in sizes.split()] == [
         ctypes.sizeof(_native.SrsRow), ctypes.sizeof(_native.SrsRng),
         ctypes.sizeof(_native.SrsAdamWHparams), ctypes.sizeof(_native.SrsSgdmHparams)]
@@ -73,7 +80,7 @@ int main(void) {{
 
 def test_library_information_without_a_gpu():
     lib = _native.load_library()
-    assert lib.srs_abi_version() == 5
+    assert lib.srs_abi_version() == 6
     assert lib.srs_tile_elems() == 2048
 
 
