@@ -87,11 +87,14 @@ def parse_args(argv=None):
                         default="adamw-8b")
     parser.add_argument("--exchange-elems", type=int, default=1 << 26,
                         help="parameters of the nvlink-exchange workload")
-    parser.add_argument("--gather", choices=("auto", "fused", "copy", "nccl", "multicast"),
+    parser.add_argument("--gather", choices=("auto", "fused", "copy", "nccl", "multicast",
+                                             "hybrid"),
                         default="auto",
                         help="how the sharded step reassembles the parameters at N>1")
     parser.add_argument("--chunks", type=int, default=32,
-                        help="tile chunks of the pipelined exchange (--gather copy)")
+                        help="tile chunks of the pipelined exchange (--gather copy, hybrid)")
+    parser.add_argument("--copy-peers", type=int, default=1,
+                        help="peers served by the copy engines (--gather hybrid)")
     parser.add_argument("--cast-elems", type=int, default=1 << 30,
                         help="elements of the cast workload (FP32 input)")
     return parser.parse_args(argv)
@@ -197,7 +200,8 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload --
 
-def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunks=32):
+def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunks=32,
+                   copy_peers=1):
     """Flat BF16 parameter and gradient buffers holding the 291 tensors; the
     optimizer (ZeRO-1 when world > 1) over views of them."""
     import torch
@@ -226,7 +230,7 @@ def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunk
     # host-streamed step of the e2e measurement loads into.
     opt = ZeroAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WEIGHT_DECAY,
                     state_format=fmt, seed=SEED, gather=gather, chunks=chunks,
-                    grads="reduce_scatter", record_timings=True)
+                    grads="reduce_scatter", record_timings=True, copy_peers=copy_peers)
     flat_g = opt.flat_grads(torch.bfloat16)
     flat_g.normal_(0, 1e-4, generator=gen)
     return opt, names, params, flat_p, flat_g, total
@@ -593,7 +597,8 @@ def run_b200(args):
     world, rank = init_distributed(args.gpus)
     peak, peak_source = measured_hbm_peak()
     opt, names, params, flat_p, flat_g, total = build_workload(
-        world, rank, args.layers, not args.no_embeddings, args.gather, args.chunks)
+        world, rank, args.layers, not args.no_embeddings, args.gather, args.chunks,
+        args.copy_peers)
     local = opt.local_numel()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -628,6 +633,9 @@ def run_b200(args):
                    "exp_avg_sq": "bfloat16 stochastic", "parallelism": f"zero1-dp{world}",
                    "gather": {"fused": "updated parameters stored into every peer replica by "
                                        "the step kernel (NVLink peer stores)",
+                              "hybrid": "the step's tile ranges store the updated parameters "
+                                        "into all peer replicas but one; the copy engines send "
+                                        "each finished range to that one",
                               "multicast": "each updated vector stored once by the step kernel "
                                            "to an NVLink multicast address (multimem.st); "
                                            "NVSwitch delivers it to every replica",

@@ -210,16 +210,20 @@ int srs_sgdm_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, 
  * [tile_lo, tile_hi) of the table only (0 <= tile_lo <= tile_hi <= n_tiles):
  * a sharded step split into chunks, each chunk's updated parameters sent to
  * the peers by srs_copy_async (a device-to-device cudaMemcpyAsync, done by
- * the copy engines) while the next chunk is updated.
+ * the copy engines) while the next chunk is updated.  `peers` (may be NULL)
+ * are replicas the range's kernel stores to itself, as in the *_gather entry
+ * points, so some peers can be served by the kernel and others by the copy
+ * engines.
  */
 int srs_adamw_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
                           int64_t tile_hi, int m_format, int m_rule, int v_format, int v_rule,
                           const srs_adamw_hparams* hp, const srs_rng* rng, uint32_t uniform_kind,
-                          int grid_ctas, void* stream);
+                          const srs_peers* peers, int grid_ctas, void* stream);
 
 int srs_sgdm_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
                          int64_t tile_hi, int u_format, int u_rule, const srs_sgdm_hparams* hp,
-                         const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream);
+                         const srs_rng* rng, uint32_t uniform_kind, const srs_peers* peers,
+                         int grid_ctas, void* stream);
 
 int srs_copy_async(void* dst, const void* src, uint64_t bytes, void* stream);
 

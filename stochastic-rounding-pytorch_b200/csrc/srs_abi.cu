@@ -383,16 +383,17 @@ int srs_sgdm_multi_gather(const srs_row* rows, int64_t n_rows, int64_t n_tiles, 
 int srs_adamw_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
                           int64_t tile_hi, int m_format, int m_rule, int v_format, int v_rule,
                           const srs_adamw_hparams* hp, const srs_rng* rng, uint32_t uniform_kind,
-                          int grid_ctas, void* stream) {
+                          const srs_peers* peers, int grid_ctas, void* stream) {
   return adamw_multi(rows, n_rows, n_tiles, m_format, m_rule, v_format, v_rule, hp, rng,
-                     uniform_kind, nullptr, grid_ctas, stream, "srs_adamw_multi_range launch",
+                     uniform_kind, peers, grid_ctas, stream, "srs_adamw_multi_range launch",
                      tile_lo, tile_hi);
 }
 
 int srs_sgdm_multi_range(const srs_row* rows, int64_t n_rows, int64_t n_tiles, int64_t tile_lo,
                          int64_t tile_hi, int u_format, int u_rule, const srs_sgdm_hparams* hp,
-                         const srs_rng* rng, uint32_t uniform_kind, int grid_ctas, void* stream) {
-  return sgdm_multi(rows, n_rows, n_tiles, u_format, u_rule, hp, rng, uniform_kind, nullptr,
+                         const srs_rng* rng, uint32_t uniform_kind, const srs_peers* peers,
+                         int grid_ctas, void* stream) {
+  return sgdm_multi(rows, n_rows, n_tiles, u_format, u_rule, hp, rng, uniform_kind, peers,
                     grid_ctas, stream, "srs_sgdm_multi_range launch", tile_lo, tile_hi);
 }
 

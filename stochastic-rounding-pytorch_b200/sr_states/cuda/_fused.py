@@ -126,7 +126,8 @@ def adamw_group_step(optimizer, group, formats, items, rng_step) -> None:
             if exchange is not None:
                 exchange.run(launch, lambda lo, hi, launch=launch, hp=hp: launcher.adamw_multi(
                     launch.table, launch.table.n_rows, launch.table.n_tiles, m_fmt, m_rule,
-                    v_fmt, v_rule, hp, rng, _stream(launch.device), tiles=(lo, hi)), whole)
+                    v_fmt, v_rule, hp, rng, _stream(launch.device), tiles=(lo, hi),
+                    **_peers_of(optimizer)), whole)
             else:
                 whole()
     if steps is None:
@@ -166,7 +167,7 @@ def sgdm_group_step(optimizer, group, formats, items, rng_step) -> None:
             if exchange is not None:
                 exchange.run(launch, lambda lo, hi, launch=launch: launcher.sgdm_multi(
                     launch.table, launch.table.n_rows, launch.table.n_tiles, u_fmt, u_rule, hp,
-                    rng, _stream(launch.device), tiles=(lo, hi)), whole)
+                    rng, _stream(launch.device), tiles=(lo, hi), **_peers_of(optimizer)), whole)
             else:
                 whole()
     if fresh:

@@ -116,11 +116,13 @@ _SIGNATURES = {
     "srs_adamw_multi_range": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                ctypes.c_int, ctypes.POINTER(SrsAdamWHparams),
-                               ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.c_int, _P],
+                               ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.POINTER(SrsPeers),
+                               ctypes.c_int, _P],
                               ctypes.c_int),
     "srs_sgdm_multi_range": ([_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                               ctypes.c_int, ctypes.c_int, ctypes.POINTER(SrsSgdmHparams),
-                              ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.c_int, _P],
+                              ctypes.POINTER(SrsRng), ctypes.c_uint32, ctypes.POINTER(SrsPeers),
+                              ctypes.c_int, _P],
                              ctypes.c_int),
     "srs_copy_async": ([_P, _P, ctypes.c_uint64, _P], ctypes.c_int),
     "srs_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
@@ -222,7 +224,9 @@ class NativeLauncher:
             _check(lib.srs_adamw_multi_range(table.device_ptr, n_rows, n_tiles, tiles[0],
                                              tiles[1], m_fmt, m_rule, v_fmt, v_rule,
                                              ctypes.byref(hp), ctypes.byref(rng),
-                                             table.uniform_kind, grid_ctas, stream))
+                                             table.uniform_kind,
+                                             None if peers is None else ctypes.byref(peers),
+                                             grid_ctas, stream))
         elif peers is None:
             _check(lib.srs_adamw_multi(table.device_ptr, n_rows, n_tiles, m_fmt, m_rule, v_fmt,
                                        v_rule, ctypes.byref(hp), ctypes.byref(rng),
@@ -239,7 +243,9 @@ class NativeLauncher:
         if tiles is not None:
             _check(lib.srs_sgdm_multi_range(table.device_ptr, n_rows, n_tiles, tiles[0], tiles[1],
                                             u_fmt, u_rule, ctypes.byref(hp), ctypes.byref(rng),
-                                            table.uniform_kind, grid_ctas, stream))
+                                            table.uniform_kind,
+                                            None if peers is None else ctypes.byref(peers),
+                                            grid_ctas, stream))
         elif peers is None:
             _check(lib.srs_sgdm_multi(table.device_ptr, n_rows, n_tiles, u_fmt, u_rule,
                                       ctypes.byref(hp), ctypes.byref(rng), table.uniform_kind,

@@ -24,6 +24,9 @@ all-gather per flat buffer after the update (``gather="nccl"`` selects it).
 memory and binds them to an NVLink multicast object: the kernel then writes
 each updated vector once (``multimem.st``) and NVSwitch delivers it to every
 replica; without multicast support it falls back to the peer stores.
+``gather="hybrid"`` splits the peers: the step's tile ranges store to all
+but ``copy_peers`` of them, and the copy engines send each finished range to
+the rest, so the kernel's stores and the copy engines share the exchange.
 ``gather="copy"`` instead runs the step over ``chunks`` tile ranges and lets
 the copy engines send each finished range to the peers while the next one is
 updated.  The default, ``"auto"``, takes ``"copy"`` with one peer and
@@ -286,10 +289,10 @@ class _ZeroMixin:
     """ZeRO-1 behaviour for a fused StateOptimizer subclass (see module docstring)."""
 
     def __init__(self, params, *args, process_group=None, gather="auto", chunks=32,
-                 grads="full", record_timings=False, **kwargs):
-        if gather not in ("auto", "fused", "copy", "nccl", "multicast"):
-            raise ValueError("gather must be 'auto', 'fused', 'copy', 'nccl' or 'multicast', "
-                             f"got {gather!r}")
+                 grads="full", record_timings=False, copy_peers=1, **kwargs):
+        if gather not in ("auto", "fused", "copy", "nccl", "multicast", "hybrid"):
+            raise ValueError("gather must be 'auto', 'fused', 'copy', 'nccl', 'multicast' or "
+                             f"'hybrid', got {gather!r}")
         if grads not in ("full", "reduce_scatter"):
             raise ValueError(f"grads must be 'full' or 'reduce_scatter', got {grads!r}")
         super().__init__(params, *args, **kwargs)
@@ -333,15 +336,22 @@ class _ZeroMixin:
             multicast = self._connect_multicast() if gather == "multicast" else None
             if multicast is not None:
                 self._srs_peers = multicast
-            elif gather in ("fused", "copy", "multicast"):
+            elif gather in ("fused", "copy", "multicast", "hybrid"):
                 connected = self._connect_peers()
                 if connected is not None and gather in ("fused", "multicast"):
                     self._srs_peers = connected[0]
-                elif connected is not None:
+                elif connected is not None and gather == "hybrid" and self._world > 2:
+                    kernel_peers, copy_starts = _split_peers(*connected, copy_peers)
+                    self._srs_peers = kernel_peers
+                    self._srs_exchange = _ChunkedExchange(self._layout, copy_starts, device,
+                                                          chunks)
+                elif connected is not None:  # "copy", or "hybrid" with a single peer
                     self._srs_exchange = _ChunkedExchange(self._layout, connected[1], device,
                                                           chunks)
         if self._world == 1:
             self._gather = "none"
+        elif self._srs_peers is not None and self._srs_exchange is not None:
+            self._gather = "hybrid"
         elif self._srs_peers is not None:
             self._gather = ("multicast" if self._srs_peers.mode == _peers_multicast()
                             else "fused")
@@ -354,8 +364,9 @@ class _ZeroMixin:
     def gather_mode(self) -> str:
         """'fused' (peer stores inside the step), 'multicast' (one NVLink
         multicast store per vector inside the step), 'copy' (copy engines
-        pipelined with the step), 'nccl' (all-gather after it) or 'none' (one
-        rank)."""
+        pipelined with the step), 'hybrid' (the step's tile ranges store to
+        some peers, the copy engines serve the others), 'nccl' (all-gather
+        after it) or 'none' (one rank)."""
         return self._gather
 
     def set_gather_mode(self, mode: str) -> None:
@@ -723,7 +734,7 @@ class _ZeroMixin:
         stream = (torch.cuda.current_stream()
                   if self._record_timings and torch.cuda.is_available() else None)
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if stream else None
-        fused = self._gather in ("fused", "copy", "multicast")
+        fused = self._gather in ("fused", "copy", "multicast", "hybrid")
         if marks:
             marks[0].record(stream)
         if fused:
@@ -866,7 +877,7 @@ class _ZeroMixin:
         self._srs_peers = None
         self._srs_exchange = None
         self._host_pipeline = None
-        if self._gather in ("fused", "copy", "multicast"):
+        if self._gather in ("fused", "copy", "multicast", "hybrid"):
             self._gather = "nccl"  # a later step all-gathers
         # The multicast bindings (self._symm_handles) stay: the parameters live in
         # those buffers.  They are released with the buffers, normally at exit.
@@ -890,6 +901,23 @@ class ZeroAdamW(_ZeroMixin, AdamWReferenceSR):
 
 class ZeroSGDM(_ZeroMixin, SGDMReferenceSR):
     """Momentum SGD (fused, sm_100a) with ZeRO-1 sharded states."""
+
+
+def _split_peers(peers, starts, copy_peers):
+    """(kernel peers, {dtype: copy-engine peer starts}) from the connected
+    peers in rotated order: the last ``copy_peers`` of them (at least one, at
+    most all but one) go to the copy engines, the rest to the kernel's stores."""
+    from .cuda import _native
+
+    n = peers.n_peers
+    k = min(max(int(copy_peers), 1), n - 1)
+    kernel = _native.SrsPeers()
+    kernel.mode = peers.mode
+    kernel.n_peers = n - k
+    for i in range(n - k):
+        kernel.delta_f32[i] = peers.delta_f32[i]
+        kernel.delta_bf16[i] = peers.delta_bf16[i]
+    return kernel, {dtype: list(s[n - k:]) for dtype, s in starts.items()}
 
 
 def _symmetric_zeros(numel, dtype, device):

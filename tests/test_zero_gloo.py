@@ -422,3 +422,21 @@ def test_bench_verification_passes_sharded_steps_and_reports_a_planted_mistake()
     wrong state byte on one rank is reported."""
     results = _spawn(_verify_worker, 2)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def test_hybrid_split_gives_the_last_peers_to_the_copy_engines():
+    from sr_states.cuda import _native
+    from sr_states.distributed import _split_peers
+
+    peers = _native.SrsPeers()
+    peers.n_peers = 7
+    for i in range(7):
+        peers.delta_bf16[i] = 1000 * (i + 1)
+        peers.delta_f32[i] = -1000 * (i + 1)
+    starts = {torch.bfloat16: [10 * (i + 1) for i in range(7)]}
+    for k, kept in ((1, 6), (3, 4), (0, 6), (9, 1)):
+        kernel, copies = _split_peers(peers, starts, k)
+        assert kernel.n_peers == kept
+        assert [kernel.delta_bf16[i] for i in range(kept)] == [1000 * (i + 1) for i in range(kept)]
+        assert [kernel.delta_f32[i] for i in range(kept)] == [-1000 * (i + 1) for i in range(kept)]
+        assert copies[torch.bfloat16] == [10 * (i + 1) for i in range(kept, 7)]
