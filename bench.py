@@ -82,6 +82,8 @@ def parse_args(argv=None):
     parser.add_argument("--no-embeddings", action="store_true",
                         help="drop the two 128256x4096 matrices (profiling case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-secondary", action="store_true",
+                        help="skip the config-3 SGDM and config-2 cast lines of the default run")
     parser.add_argument("--workload", choices=("adamw-8b", "sgdm-gpt2", "cast", "adamw-70b",
                                                "nvlink-exchange"),
                         default="adamw-8b")
@@ -591,6 +593,23 @@ def split_phase(opt, steps, world, stream):
             max_over_ranks(statistics.mean(t["gather_ms"] for t in timings), world))
 
 
+def secondary_workloads(args):
+    """BASELINE configs 3 and 2 measured in the same run as the headline (one
+    GPU, after it): the GPT-2-small SGDM step and the 2^30-element casts, each
+    with its roofline and clocks, so their numbers come from the same timed
+    command as the headline."""
+    sub = argparse.Namespace(**{**vars(args), "steps": max(args.steps, 10),
+                                "warmup": max(args.warmup, 3)})
+    keep = ("value", "unit", "ms_per_step", "step_ms_min", "roofline", "clocks", "gpu_launches")
+    sgdm = measure_sgdm_gpt2(sub)
+    casts = measure_casts(sub)
+    return {
+        "sgdm_gpt2": {"workload": sgdm["config"]["workload"], **{k: sgdm[k] for k in keep
+                                                                  if k in sgdm}},
+        "casts": [{"workload": c["config"]["workload"], "elements": c["config"]["elements"],
+                   **{k: c[k] for k in keep if k in c}} for c in casts]}
+
+
 def run_b200(args):
     import torch
 
@@ -678,6 +697,8 @@ def run_b200(args):
         line.pop("verify")
     if not args.no_e2e:
         line["e2e"] = e2e_run(opt, flat_p, flat_g, args.e2e_steps, world, total)
+    if world == 1 and not args.no_secondary:
+        line["secondary"] = secondary_workloads(args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_reference_subprocess(args) or cpu_baseline(args.cpu_seconds)
         line["cpu_baseline"]["port"] = cpu_baseline(min(args.cpu_seconds, 4.0))
@@ -691,6 +712,10 @@ def run_b200(args):
 
 
 def run_sgdm_gpt2(args):
+    print(json.dumps(measure_sgdm_gpt2(args)), flush=True)
+
+
+def measure_sgdm_gpt2(args):
     """Momentum SGD at the GPT-2-small shape on one GPU."""
     import torch
 
@@ -716,7 +741,7 @@ def run_sgdm_gpt2(args):
         offset += n
     opt = ZeroSGDM(params, lr=1e-2, momentum=0.9,
                    state_format={"momentum_buffer": StateFormat(torch.bfloat16, "stochastic")},
-                   seed=11)
+                   seed=11, record_timings=True)
     for _ in range(args.warmup):
         opt.step()
     torch.cuda.synchronize()
@@ -728,7 +753,8 @@ def run_sgdm_gpt2(args):
     kernel_ms = statistics.mean(t["update_ms"] for t in opt.timings)
     bytes_per_param = 16  # read p (4), g (4), u (2); write p (4), u (2)
     achieved = bytes_per_param * total / (kernel_ms / 1e3) / 1e9
-    print(json.dumps({
+    opt.close()
+    return {
         "metric": "SGDM-SR step params/sec & HBM GB/s at GPT-2-small shape", "value":
         total / (ms / 1e3), "unit": "params/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -743,10 +769,15 @@ def run_sgdm_gpt2(args):
                      "kernel": "srs::sgdm_kernel<BF16>", "kernel_ms": kernel_ms,
                      "bytes_per_param": bytes_per_param},
         "step_ms_min": min(per_step), "gpu_launches": opt.launches_per_step() * args.steps,
-        "clocks": clocks.report()}), flush=True)
+        "clocks": clocks.report()}
 
 
 def run_cast(args):
+    for line in measure_casts(args):
+        print(json.dumps(line), flush=True)
+
+
+def measure_casts(args):
     """The standalone cast of FP32 data: magnitudes 2^U(-20, 18)
     with random signs; one line per target format and rule at --cast-elems."""
     import torch
@@ -760,6 +791,7 @@ def run_cast(args):
     x = torch.empty(n, device=device).uniform_(-20, 18, generator=gen).exp2_()
     x *= torch.empty(n, device=device).bernoulli_(0.5, generator=gen).mul_(2).sub_(1)
     stream = torch.cuda.current_stream()
+    lines = []
     for dtype, size in ((torch.bfloat16, 2), (torch.float16, 2), (torch.float8_e4m3fn, 1),
                         (torch.float8_e5m2, 1)):
         for rule in ("stochastic", "nearest"):
@@ -781,7 +813,7 @@ def run_cast(args):
                 torch.cuda.synchronize()
             ms = start.elapsed_time(end) / args.steps
             achieved = (4 + size) * n / (ms / 1e3) / 1e9
-            print(json.dumps({
+            lines.append({
                 "metric": "cast elements/sec & HBM GB/s", "value": n / (ms / 1e3),
                 "unit": "elements/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -792,8 +824,10 @@ def run_cast(args):
                              "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                              "peak_source": peak_source, "kernel": "srs::cast_kernel",
                              "bytes_per_elem": 4 + size},
-                "gpu_launches": args.steps, "clocks": clocks.report()}), flush=True)
+                "gpu_launches": args.steps, "clocks": clocks.report()})
             del out
+    del x
+    return lines
 
 
 def run_adamw_70b(args):
