@@ -54,11 +54,11 @@ METRIC = "AdamW-SR step params/sec & HBM GB/s (% of peak) at 8B shape, 1/2/4/8 B
 # (BF16 p/g = 2 B, E4M3 m = 1 B, BF16 v = 2 B): 2+2+1+2 + 2+1+2 = 12.
 BYTES_PER_PARAM = 12
 # DRAM bytes per parameter of one AdamW launch measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum = 5.197 GB over the 436,228,096
+# (dram__bytes_read.sum + dram__bytes_write.sum = 5.188656 GB over the 436,228,096
 # parameters of the 2-layer profiling case; profiles/adamw_kernel_llama3-8b.md).
 # Traffic grows in proportion to the parameters, so a full launch moves this
 # many bytes per parameter.
-MEASURED_TRAFFIC_PER_PARAM = 11.913
+MEASURED_TRAFFIC_PER_PARAM = 11.894
 FALLBACK_HBM_GBS = 6650.0
 # BASELINE config 4 hyperparameters.
 LR, BETAS, EPS, WEIGHT_DECAY, SEED = 3e-4, (0.9, 0.999), 1e-8, 0.1, 7
@@ -564,11 +564,46 @@ def e2e_run(opt, flat_p, flat_g, steps, world, total):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
+    link = pcie_rates(host_g, host_p, flat_g, world)
+    moved = shard * 2 / (ms / 1e3) / 1e9  # each direction
     return {"value": total / (ms / 1e3), "unit": "params/s", "ms_per_step": ms,
             "h2d_bytes_per_step": shard * 2, "d2h_bytes_per_step": shard * 2,
+            "pcie": {"achieved_gbs_per_direction": moved, **link,
+                     "frac": moved / min(link["h2d_gbs"], link["d2h_gbs"]),
+                     "how": "peak: 2 GiB pinned copies in both directions at once on two "
+                            "streams, CUDA events, best of 3, all ranks copying together"},
             "api": "ZeroAdamW.step_host (pinned host gradients in, parameters out)" + (
                 f"; each of the {world} ranks loads its own gradient shard and sends back its "
                 "own updated parameter shard (bytes above are per rank)" if world > 1 else "")}
+
+
+def pcie_rates(host_g, host_p, device_buffer, world):
+    """Host<->device copy bandwidth in each direction with both running at once
+    (as in the host-streamed step), from this rank's pinned buffers."""
+    import torch
+
+    n = min(host_g.numel(), host_p.numel(), device_buffer.numel(), 1 << 30)  # 2 GiB of BF16
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    scratch = torch.empty(n, dtype=torch.bfloat16, device=device_buffer.device)
+    best = (0.0, 0.0)
+    for _ in range(3):
+        barrier(world)
+        torch.cuda.synchronize()
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        marks[0].record(up)
+        marks[2].record(down)
+        with torch.cuda.stream(up):
+            scratch.copy_(host_g[:n], non_blocking=True)
+        with torch.cuda.stream(down):
+            host_p[:n].copy_(device_buffer[:n], non_blocking=True)
+        marks[1].record(up)
+        marks[3].record(down)
+        torch.cuda.synchronize()
+        rates = (2 * n / (marks[0].elapsed_time(marks[1]) / 1e3) / 1e9,
+                 2 * n / (marks[2].elapsed_time(marks[3]) / 1e3) / 1e9)
+        best = max(best, rates, key=lambda r: min(r))
+    del scratch
+    return {"h2d_gbs": best[0], "d2h_gbs": best[1]}
 
 
 def split_phase(opt, steps, world, stream):
