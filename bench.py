@@ -97,6 +97,8 @@ def parse_args(argv=None):
                         help="tile chunks of the pipelined exchange (--gather copy, hybrid)")
     parser.add_argument("--copy-peers", type=int, default=1,
                         help="peers served by the copy engines (--gather hybrid)")
+    parser.add_argument("--copy-streams", type=int, default=None,
+                        help="copy streams of the copy-engine exchange (default: one per peer)")
     parser.add_argument("--cast-elems", type=int, default=1 << 30,
                         help="elements of the cast workload (FP32 input)")
     return parser.parse_args(argv)
@@ -203,7 +205,7 @@ class ClockSampler:
 # -------------------------------------------------------------- workload --
 
 def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunks=32,
-                   copy_peers=1):
+                   copy_peers=1, copy_streams=None):
     """Flat BF16 parameter and gradient buffers holding the 291 tensors; the
     optimizer (ZeRO-1 when world > 1) over views of them."""
     import torch
@@ -232,7 +234,8 @@ def build_workload(world, rank, layers=32, embeddings=True, gather="auto", chunk
     # host-streamed step of the e2e measurement loads into.
     opt = ZeroAdamW(params, lr=LR, betas=BETAS, eps=EPS, weight_decay=WEIGHT_DECAY,
                     state_format=fmt, seed=SEED, gather=gather, chunks=chunks,
-                    grads="reduce_scatter", record_timings=True, copy_peers=copy_peers)
+                    grads="reduce_scatter", record_timings=True, copy_peers=copy_peers,
+                    copy_streams=copy_streams)
     flat_g = opt.flat_grads(torch.bfloat16)
     flat_g.normal_(0, 1e-4, generator=gen)
     return opt, names, params, flat_p, flat_g, total
@@ -652,7 +655,7 @@ def run_b200(args):
     peak, peak_source = measured_hbm_peak()
     opt, names, params, flat_p, flat_g, total = build_workload(
         world, rank, args.layers, not args.no_embeddings, args.gather, args.chunks,
-        args.copy_peers)
+        args.copy_peers, args.copy_streams)
     local = opt.local_numel()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):

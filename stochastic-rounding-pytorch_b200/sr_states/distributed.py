@@ -179,13 +179,17 @@ class _ChunkedExchange:
     with ``whole=True`` keeps one full launch (the fused peer stores need it)
     and only brackets it with the host copies."""
 
-    def __init__(self, layout, peer_starts, device, chunks=32, whole=False):
+    def __init__(self, layout, peer_starts, device, chunks=32, whole=False, copy_streams=None):
         self._layout = layout
         self._peer_starts = peer_starts or {}  # dtype -> start of each peer's buffer, here
         self._chunks = 1 if whole else chunks
         self._whole = whole
         n_peers = len(next(iter(peer_starts.values()))) if peer_starts else 0
-        self._streams = [torch.cuda.Stream(device) for _ in range(n_peers)]
+        # Copy streams: one per peer by default; fewer serialise the peers of a
+        # chunk on each stream (peer w goes to stream w % copy_streams).
+        n_streams = n_peers if copy_streams is None else max(1, min(int(copy_streams), n_peers))
+        self._streams = [torch.cuda.Stream(device) for _ in range(n_streams if n_peers else 0)]
+        self._n_peers = n_peers
         self._device = device
         self._host_streams = None
         self.host: _HostIO | None = None  # set for the duration of a step_host call
@@ -266,8 +270,10 @@ class _ChunkedExchange:
                 launch_tiles(lo, hi)
             done = torch.cuda.Event()
             done.record(compute)
-            for w, stream in enumerate(self._streams):
+            for stream in self._streams:
                 stream.wait_event(done)
+            for w in range(self._n_peers):
+                stream = self._streams[w % len(self._streams)]
                 for dtype, start, nbytes in runs:
                     local = self._layout.buffers[dtype].data_ptr()
                     launcher.copy_async(self._peer_starts[dtype][w] + (start - local), start,
@@ -289,7 +295,8 @@ class _ZeroMixin:
     """ZeRO-1 behaviour for a fused StateOptimizer subclass (see module docstring)."""
 
     def __init__(self, params, *args, process_group=None, gather="auto", chunks=32,
-                 grads="full", record_timings=False, copy_peers=1, **kwargs):
+                 grads="full", record_timings=False, copy_peers=1, copy_streams=None,
+                 **kwargs):
         if gather not in ("auto", "fused", "copy", "nccl", "multicast", "hybrid"):
             raise ValueError("gather must be 'auto', 'fused', 'copy', 'nccl', 'multicast' or "
                              f"'hybrid', got {gather!r}")
@@ -344,10 +351,10 @@ class _ZeroMixin:
                     kernel_peers, copy_starts = _split_peers(*connected, copy_peers)
                     self._srs_peers = kernel_peers
                     self._srs_exchange = _ChunkedExchange(self._layout, copy_starts, device,
-                                                          chunks)
+                                                          chunks, copy_streams=copy_streams)
                 elif connected is not None:  # "copy", or "hybrid" with a single peer
                     self._srs_exchange = _ChunkedExchange(self._layout, connected[1], device,
-                                                          chunks)
+                                                          chunks, copy_streams=copy_streams)
         if self._world == 1:
             self._gather = "none"
         elif self._srs_peers is not None and self._srs_exchange is not None:
