@@ -733,6 +733,18 @@ def run_b200(args):
     line["verify"] = verify_step(opt, names, params, world, rank)
     if rank != 0:
         line.pop("verify")
+    if world >= 4 and not args.no_secondary:
+        # BASELINE config 5 (70B, everything sharded) where every rank has room.
+        if adamw_70b_fits(world):
+            sub = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 5),
+                                        "warmup": min(args.warmup, 2)})
+            big = measure_adamw_70b(sub, world, rank)
+            line["secondary"] = {"adamw_70b": {
+                "workload": big["config"]["workload"], "parallelism": big["config"]["parallelism"],
+                **{k: big[k] for k in ("value", "unit", "ms_per_step", "roofline", "gather_ms",
+                                       "clocks", "gpu_launches")}}}
+        else:
+            line["secondary"] = {"adamw_70b": "skipped: not enough free memory on every rank"}
     if not args.no_e2e:
         line["e2e"] = e2e_run(opt, flat_p, flat_g, args.e2e_steps, world, total)
     if world == 1 and not args.no_secondary:
@@ -892,6 +904,37 @@ def run_adamw_70b(args):
     world, rank = init_distributed(args.gpus)
     if world < 4:
         raise SystemExit("the 70B workload needs at least 4 GPUs (memory)")
+    line = measure_adamw_70b(args, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
+ADAMW_70B_BYTES_PER_PARAM = 8  # per rank: BF16 parameter and gradient, FP16 moments
+
+
+def adamw_70b_fits(world):
+    """Whether every rank has room for its 70B shard (parameters, gradients and
+    FP16 states of 70,553,706,496 / world parameters, plus the 16 GB staging
+    buffer and 8 GB of headroom); agreed over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    need = 70_553_706_496 // world * ADAMW_70B_BYTES_PER_PARAM + 24 * 10**9
+    free = torch.tensor([torch.cuda.mem_get_info()[0]], dtype=torch.int64, device="cuda")
+    dist.all_reduce(free, op=dist.ReduceOp.MIN)
+    return int(free.item()) >= need
+
+
+def measure_adamw_70b(args, world, rank):
+    import torch
+    import torch.distributed as dist
+
+    from sr_states.cuda import _native
+    from sr_states.cuda._fused import adamw_hparams, rng_words
+    from sr_states.cuda._tables import DeviceTable, Update, build_table, upload
+    from sr_states.shapes import llama3_70b
+
     peak, peak_source = measured_hbm_peak()
     shapes = [s for _, s in llama3_70b()]
     ordered = [s for s in shapes if len(s) == 1] + [s for s in shapes if len(s) > 1]
@@ -989,9 +1032,10 @@ def run_adamw_70b(args):
                      "bytes_per_param": bytes_per_param, "params_per_launch": shard},
         "gather_ms": gather_ms, "gpu_launches": sum(t is not None for t in tables) * args.steps,
         "clocks": clocks.report()}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    dist.destroy_process_group()
+    del p, g, m, v, staging, tables
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return line
 
 
 def run_nvlink_exchange(args):
