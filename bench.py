@@ -79,6 +79,9 @@ def parse_args(argv=None):
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--layers", type=int, default=32,
                         help="decoder layers of the Llama-3-8B shape (profiling uses fewer)")
+    parser.add_argument("--layers-70b", type=int, default=80,
+                        help="decoder layers of the Llama-3-70B shape (config 5; fewer only to "
+                             "check the workload on fewer GPUs)")
     parser.add_argument("--no-embeddings", action="store_true",
                         help="drop the two 128256x4096 matrices (profiling case)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -735,10 +738,10 @@ def run_b200(args):
         line.pop("verify")
     if world >= 4 and not args.no_secondary:
         # BASELINE config 5 (70B, everything sharded) where every rank has room.
-        if adamw_70b_fits(world):
+        if adamw_70b_fits(world, args.layers_70b):
             sub = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 5),
                                         "warmup": min(args.warmup, 2)})
-            big = measure_adamw_70b(sub, world, rank)
+            big = measure_adamw_70b(sub, world, rank, args.layers_70b)
             line["secondary"] = {"adamw_70b": {
                 "workload": big["config"]["workload"], "parallelism": big["config"]["parallelism"],
                 **{k: big[k] for k in ("value", "unit", "ms_per_step", "roofline", "gather_ms",
@@ -893,18 +896,13 @@ def run_adamw_70b(args):
     rank's rows (one launch per group) followed by the all-gather of the
     updated parameters, in chunks through one reused 16 GB staging buffer (the
     way a sharded model streams its parameters); both are timed."""
-    import torch
     import torch.distributed as dist
 
-    from sr_states.cuda import _native
-    from sr_states.cuda._fused import adamw_hparams, rng_words
-    from sr_states.cuda._tables import DeviceTable, Update, build_table, upload
-    from sr_states.shapes import llama3_70b
-
     world, rank = init_distributed(args.gpus)
-    if world < 4:
-        raise SystemExit("the 70B workload needs at least 4 GPUs (memory)")
-    line = measure_adamw_70b(args, world, rank)
+    if not adamw_70b_fits(world, args.layers_70b):
+        raise SystemExit("not enough device memory on every rank for this 70B shard "
+                         "(the full model needs at least 4 GPUs)")
+    line = measure_adamw_70b(args, world, rank, args.layers_70b)
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
@@ -913,30 +911,37 @@ def run_adamw_70b(args):
 ADAMW_70B_BYTES_PER_PARAM = 8  # per rank: BF16 parameter and gradient, FP16 moments
 
 
-def adamw_70b_fits(world):
+def llama3_70b_shapes(layers=80):
+    """The Llama-3-70B parameter shapes, optionally with fewer decoder layers."""
+    from sr_states.shapes import _llama
+
+    return [s for _, s in _llama(layers, 8192, 8 * 128, 28672)]
+
+
+def adamw_70b_fits(world, layers=80):
     """Whether every rank has room for its 70B shard (parameters, gradients and
-    FP16 states of 70,553,706,496 / world parameters, plus the 16 GB staging
+    FP16 states of the model's parameters / world, plus the 16 GB staging
     buffer and 8 GB of headroom); agreed over the ranks."""
     import torch
     import torch.distributed as dist
 
-    need = 70_553_706_496 // world * ADAMW_70B_BYTES_PER_PARAM + 24 * 10**9
+    total = sum(math.prod(s) for s in llama3_70b_shapes(layers))
+    need = total // world * ADAMW_70B_BYTES_PER_PARAM + 24 * 10**9
     free = torch.tensor([torch.cuda.mem_get_info()[0]], dtype=torch.int64, device="cuda")
     dist.all_reduce(free, op=dist.ReduceOp.MIN)
     return int(free.item()) >= need
 
 
-def measure_adamw_70b(args, world, rank):
+def measure_adamw_70b(args, world, rank, layers=80):
     import torch
     import torch.distributed as dist
 
     from sr_states.cuda import _native
     from sr_states.cuda._fused import adamw_hparams, rng_words
     from sr_states.cuda._tables import DeviceTable, Update, build_table, upload
-    from sr_states.shapes import llama3_70b
 
     peak, peak_source = measured_hbm_peak()
-    shapes = [s for _, s in llama3_70b()]
+    shapes = llama3_70b_shapes(layers)
     ordered = [s for s in shapes if len(s) == 1] + [s for s in shapes if len(s) > 1]
     numels = [math.prod(s) for s in ordered]
     n_vectors = sum(1 for s in ordered if len(s) == 1)
@@ -1017,7 +1022,8 @@ def measure_adamw_70b(args, world, rank):
         "unit": "params/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama3-70b AdamW-SR optimizer step (BASELINE config 5)",
+        "config": {"workload": "llama3-70b AdamW-SR optimizer step (BASELINE config 5)"
+                               + ("" if layers == 80 else f" reduced to {layers} layers"),
                    "params": total, "tensors": len(ordered), "param_dtype": "bf16",
                    "grad_dtype": "bf16", "exp_avg": "float16 stochastic",
                    "exp_avg_sq": "float16 stochastic",
