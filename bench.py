@@ -736,8 +736,9 @@ def run_b200(args):
     line["verify"] = verify_step(opt, names, params, world, rank)
     if rank != 0:
         line.pop("verify")
-    if world >= 4 and not args.no_secondary:
-        # BASELINE config 5 (70B, everything sharded) where every rank has room.
+    if (world >= 4 or (world > 1 and args.layers_70b < 80)) and not args.no_secondary:
+        # BASELINE config 5 (70B, everything sharded) where every rank has room
+        # (a reduced layer count lets two GPUs check this path).
         if adamw_70b_fits(world, args.layers_70b):
             sub = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 5),
                                         "warmup": min(args.warmup, 2)})
