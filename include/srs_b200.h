@@ -256,7 +256,14 @@ int srs_ipc_close(void* base);
  *     gradients and 2- or 4-byte states, 8 bytes for FP8 states); a violation
  *     fails with SRS_ERR_INVALID_ARGUMENT;
  *   - the first call on a device looks up the table's address (set-up); make
- *     that first call before any stream capture;
+ *     that first call before any stream capture (a first call made during
+ *     capture fails with SRS_ERR_INVALID_ARGUMENT);
+ *   - a call captured into a CUDA graph captures the row copy too, which then
+ *     reads host_rows at every replay: under capture host_rows must be
+ *     page-locked (cudaHostAlloc / cudaHostRegister; pageable rows fail with
+ *     SRS_ERR_INVALID_ARGUMENT) and stay valid while the graph can be
+ *     replayed; a replay uses the rows' contents at that time, but the
+ *     hyperparameters and RNG words captured with the call;
  *   - calls on one device that can overlap in time (different streams or host
  *     threads without ordering) race on the shared table: order them.
  */

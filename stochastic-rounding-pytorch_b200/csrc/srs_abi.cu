@@ -571,12 +571,18 @@ srs_row* g_noalloc_table[kMaxDevices];  // device address of g_noalloc_rows, per
 
 // Set-up on a device's first call: look up where the module placed the table.
 // Module loading is lazy, so this first lookup may load the library's device
-// code; make the first call on each device before any stream capture.
-int noalloc_table(srs_row** table) {
+// code; it is refused while the stream captures (`capturing`), so the first
+// call on each device has to come before any stream capture.
+int noalloc_table(srs_row** table, bool capturing) {
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
   std::lock_guard<std::mutex> lock(g_mutex);
   if (g_noalloc_table[dev] == nullptr) {
+    if (capturing)
+      return fail(SRS_ERR_INVALID_ARGUMENT,
+                  "srs_adamw_multi_noalloc: the first call on device %d was made during stream "
+                  "capture; make one call on the device before capturing",
+                  dev);
     void* address = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&address, g_noalloc_rows);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(row table)");
@@ -669,14 +675,31 @@ extern "C" int srs_adamw_multi_noalloc(const srs_row* host_rows, int64_t n_rows,
     return rc;
   if (n_tiles == 0) return SRS_OK;
   if (int rc = check_device()) return rc;
-  srs_row* table = nullptr;
-  if (int rc = noalloc_table(&table)) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &capture);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  const bool capturing = capture != cudaStreamCaptureStatusNone;
+  if (capturing) {
+    // A captured row copy is a graph node that reads host_rows again at every
+    // replay: only page-locked rows can be copied that way, and they have to
+    // stay valid for as long as the graph can be replayed.
+    cudaPointerAttributes where{};
+    e = cudaPointerGetAttributes(&where, host_rows);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes(host_rows)");
+    if (where.type != cudaMemoryTypeHost)
+      return fail(SRS_ERR_INVALID_ARGUMENT,
+                  "srs_adamw_multi_noalloc under stream capture needs page-locked host_rows "
+                  "(every replay copies them again)");
+  }
+  srs_row* table = nullptr;
+  if (int rc = noalloc_table(&table, capturing)) return rc;
   // Stream-ordered: the kernel below (and any later call's copy on this stream)
   // sees exactly these rows.  The copy may read host_rows at any time until it
-  // has run on the stream, so the caller keeps them valid until then.
-  cudaError_t e = cudaMemcpyAsync(table, host_rows, (size_t)n_rows * sizeof(srs_row),
-                                  cudaMemcpyHostToDevice, s);
+  // has run on the stream (at every replay, when captured), so the caller keeps
+  // them valid until then.
+  e = cudaMemcpyAsync(table, host_rows, (size_t)n_rows * sizeof(srs_row),
+                      cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return cuda_fail(e, "srs_adamw_multi_noalloc row copy");
   AdamWArgs a{};
   a.hp = *hp;

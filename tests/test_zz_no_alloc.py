@@ -222,3 +222,50 @@ def test_noalloc_rejects_a_vector_flag_on_misaligned_rows():
     unflagged["flags"] = _native.ROW_PARAM_BF16 | _native.ROW_GRAD_BF16
     for good in (table, fp8_ok, unflagged):
         assert b"n_tiles" in message(good)
+
+
+@pytest.mark.gpu
+def test_noalloc_captured_into_a_graph_needs_page_locked_rows(cuda_device):
+    """Under stream capture the row copy becomes a graph node that reads
+    host_rows at every replay, so pageable rows are refused (nothing is
+    enqueued and the capture stays usable) and page-locked rows are accepted.
+    One replay of the captured step must equal the same step called directly
+    (tolerance: exact).  The refusal needs a device to ask whether the stream
+    captures, so it is checked here, not in the CPU tests."""
+    lib = _native.load_library()
+    tile = int(lib.srs_tile_elems())
+    generator = torch.Generator().manual_seed(11)
+    captured = make_rows(UNIFORM, cuda_device, generator)
+    direct = [[t.clone() for t in row] for row in captured]
+    table_captured, n_tiles = host_table(UNIFORM, captured, tile)
+    table_direct, _ = host_table(UNIFORM, direct, tile)
+    pinned = torch.from_numpy(table_captured.view(np.uint8).copy()).pin_memory()
+    hp, words = hparams((1, 2)), rng(1)
+
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    check(lib, lib.srs_adamw_multi_noalloc(table_direct.ctypes.data, len(UNIFORM), n_tiles,
+                                           E4M3, SR, BF16, SR, ctypes.byref(hp),
+                                           ctypes.byref(words), 0, stream))
+    torch.cuda.synchronize(cuda_device)
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        stream = torch.cuda.current_stream(cuda_device).cuda_stream
+        rc = lib.srs_adamw_multi_noalloc(table_captured.ctypes.data, len(UNIFORM), n_tiles,
+                                         E4M3, SR, BF16, SR, ctypes.byref(hp),
+                                         ctypes.byref(words), 0, stream)
+        refusal = lib.srs_last_error()
+        accepted = lib.srs_adamw_multi_noalloc(pinned.data_ptr(), len(UNIFORM), n_tiles, E4M3,
+                                               SR, BF16, SR, ctypes.byref(hp),
+                                               ctypes.byref(words), 0, stream)
+        message = lib.srs_last_error()
+    assert rc == _native.SRS_ERR_INVALID_ARGUMENT and b"page-locked" in refusal, refusal
+    assert accepted == _native.SRS_OK, message.decode()
+    for row in captured:  # capturing ran nothing
+        assert not bool(row[2].float().abs().sum() > 0)
+    graph.replay()
+    torch.cuda.synchronize(cuda_device)
+    for r, (a_row, b_row) in enumerate(zip(captured, direct)):
+        for name, a, b in zip(("param", "grad", "m", "v"), a_row, b_row):
+            assert np.array_equal(bits(a), bits(b)), f"row {r} {name}: replay differs"
+    del graph
