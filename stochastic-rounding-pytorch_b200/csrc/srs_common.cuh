@@ -242,8 +242,8 @@ __device__ __forceinline__ uint32_t toward_zero1(float x) {
 // NaN; for the FP16/FP8 grids every |x| < 2^63).  Vectors that fail it use the
 // per-element functions above, so results are identical either way.
 //
-// BF16: the same integer addition as bf16_stochastic; one byte permutation
-// keeps the high halves of two sums.
+// BF16: the same integer addition as bf16_stochastic, done by the hardware's
+// stochastic conversion (cvt_rs_bf16x2) for two elements at a time.
 //
 // FP16/FP8 grids, in FP32 arithmetic.  With U = 2^(max(e, emin) - M) the grid
 // step at |x| and N = (~h) >> 8, the reference's decision
@@ -469,20 +469,44 @@ __device__ __forceinline__ void encode8_stochastic_exact(const float (&x)[kVec],
   }
 }
 
-// h32 of counter c + j, one of a vector's 8 consecutive counters.  SHARED: the
+// h32 of counter c + j, one of a vector's 8 consecutive counters, before its
+// last xor-shift: h32(c + j) == u ^ (u >> 16) for the returned u.  SHARED: the
 // 8 counters do not carry across bit 16, so (c + j) >> 16 == hi for all of
 // them and the first xor-shift of h32 reuses that one shift.
 template <bool SHARED>
+__device__ __forceinline__ uint32_t h32_unmixed_at(uint32_t c, uint32_t j, uint32_t hi) {
+  uint32_t x = c + j;
+  x ^= SHARED ? hi : (x >> 16);
+  x *= 0x7FEB352Du;
+  x ^= x >> 15;
+  return x * 0x846CA68Bu;
+}
+
+template <bool SHARED>
 __device__ __forceinline__ uint32_t h32_at(uint32_t c, uint32_t j, uint32_t hi) {
-  if constexpr (SHARED) {
-    uint32_t x = (c + j) ^ hi;
-    x *= 0x7FEB352Du;
-    x ^= x >> 15;
-    x *= 0x846CA68Bu;
-    return x ^ (x >> 16);
-  } else {
-    return h32(c + j);
-  }
+  const uint32_t u = h32_unmixed_at<SHARED>(c, j, hi);
+  return u ^ (u >> 16);
+}
+
+// The random bits of two BF16 stochastic roundings in the layout of
+// cvt_rs_bf16x2: the low 16 bits of h32 are lo16(u) ^ hi16(u), so one byte
+// permutation gathers both elements' low halves, another their high halves,
+// and one xor mixes them (element `lo` in bits 0-15, element `hi` in 16-31).
+__device__ __forceinline__ uint32_t bf16x2_random_bits(uint32_t u_lo, uint32_t u_hi) {
+  return __byte_perm(u_lo, u_hi, 0x5410u) ^ __byte_perm(u_lo, u_hi, 0x7632u);
+}
+
+// sm_100a's stochastic conversion of two FP32 values to BF16: `hi` is rounded
+// with rbits[31:16] into the upper half, `lo` with rbits[15:0] into the lower
+// half, each as (FP32 encoding + its 16 random bits) >> 16 -- the rule of
+// bf16_stochastic for every input but NaN (no flush of subnormals, overflow
+// carries into infinity, infinities stay).  Checked on B200 against that rule
+// for every FP32 encoding (the screened-rounding self-test) and on random
+// pairs over the whole FP32 range.
+__device__ __forceinline__ uint32_t cvt_rs_bf16x2(float hi, float lo, uint32_t rbits) {
+  uint32_t d;
+  asm("cvt.rs.bf16x2.f32 %0, %1, %2, %3;" : "=r"(d) : "f"(hi), "f"(lo), "r"(rbits));
+  return d;
 }
 
 template <int F, bool SHARED>
@@ -492,10 +516,9 @@ __device__ __forceinline__ void encode8_stochastic_fast_as(const float (&x)[kVec
   if constexpr (F == SRS_FMT_BF16) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t lo = __float_as_uint(x[2 * i]) + (h32_at<SHARED>(ctr0, 2 * i, hi) & 0xFFFFu);
-      const uint32_t up =
-          __float_as_uint(x[2 * i + 1]) + (h32_at<SHARED>(ctr0, 2 * i + 1, hi) & 0xFFFFu);
-      w[i] = __byte_perm(lo, up, 0x7632u);
+      const uint32_t rbits = bf16x2_random_bits(h32_unmixed_at<SHARED>(ctr0, 2 * i, hi),
+                                                h32_unmixed_at<SHARED>(ctr0, 2 * i + 1, hi));
+      w[i] = cvt_rs_bf16x2(x[2 * i + 1], x[2 * i], rbits);
     }
   } else if constexpr (F == SRS_FMT_F16) {
 #pragma unroll

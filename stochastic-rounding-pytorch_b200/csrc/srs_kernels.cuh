@@ -263,6 +263,14 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
+// min(a, b, c) in one instruction (sm_100's three-input min.f32; like fminf,
+// a NaN operand is ignored).
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ float rsqrt_approx(float x) {
   float y;
   asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -296,17 +304,17 @@ __device__ __forceinline__ bool adamw_screen(const float (&m1)[kVec], const floa
 #pragma unroll
   for (int j = 0; j < kVec; ++j) y[j] = rsqrt_approx(v1[j]);
   float2 acc = mul2_rn(make_float2(m1[0], m1[1]), make_float2(m1[0], m1[1]));
-  float lo = fminf(fabsf(m1[0]), fabsf(m1[1]));
 #pragma unroll
   for (int i = 0; i < kVec / 2; ++i) {
-    if (i > 0) {
+    if (i > 0)
       acc = fma2_rn(make_float2(m1[2 * i], m1[2 * i + 1]), make_float2(m1[2 * i], m1[2 * i + 1]),
                     acc);
-      lo = fminf(lo, fminf(fabsf(m1[2 * i]), fabsf(m1[2 * i + 1])));
-    }
     acc = fma2_rn(make_float2(v1[2 * i], v1[2 * i + 1]), splat2(0x1p88f), acc);
     acc = fma2_rn(make_float2(y[2 * i], y[2 * i + 1]), splat2(0x1p86f), acc);
   }
+  const float lo = fmin3(fmin3(fabsf(m1[0]), fabsf(m1[1]), fabsf(m1[2])),
+                         fmin3(fabsf(m1[3]), fabsf(m1[4]), fabsf(m1[5])),
+                         fminf(fabsf(m1[6]), fabsf(m1[7])));
   return (acc.x + acc.y < 0x1p126f) && (lo >= m_floor);
 }
 
