@@ -156,6 +156,32 @@ def max_over_ranks(value, world):
     return float(t.item())
 
 
+def box_copy_gbs(world):
+    """This GPU's own device-copy rate (slowest rank): one 4 GiB FP32 buffer
+    copied into another (32x the L2), best of 5, CUDA events; bytes read plus
+    written per second.  Context for box-to-box differences of the kernel's
+    rate; the roofline's peak stays the pool's measured copy bandwidth."""
+    import torch
+
+    n = 1 << 30
+    src = torch.ones(n, dtype=torch.float32, device="cuda")
+    dst = torch.empty_like(src)
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        dst.copy_(src)
+    best = float("inf")
+    for _ in range(5):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        dst.copy_(src)
+        end.record(stream)
+        end.synchronize()
+        best = min(best, start.elapsed_time(end))
+    del src, dst
+    torch.cuda.empty_cache()
+    return -max_over_ranks(-(2 * 4 * n / (best / 1e3) / 1e9), world)
+
+
 # ---------------------------------------------------------------- clocks --
 
 class ClockSampler:
@@ -677,6 +703,7 @@ def run_b200(args):
         update_ms, nccl_ms = split_phase(opt, args.steps, world, stream)
     else:
         update_ms, nccl_ms = step_kernel_ms, None
+    box_copy = box_copy_gbs(world)
     achieved = BYTES_PER_PARAM * local / (update_ms / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": total / (ms / 1e3), "unit": "params/s", "n_gpus": world,
@@ -716,7 +743,12 @@ def run_b200(args):
                      "timed": "the update launch alone" + (
                          " (from the steps whose exchange is a separate NCCL all-gather)"
                          if world > 1 else ""),
-                     "bytes_per_param": BYTES_PER_PARAM, "params_per_launch": local},
+                     "bytes_per_param": BYTES_PER_PARAM, "params_per_launch": local,
+                     "box_copy_gbs": box_copy,
+                     "frac_of_box_copy": achieved / box_copy,
+                     "box_copy_how": "torch device copy of a 4 GiB FP32 buffer on this GPU "
+                                     "after the timed steps, best of 5, CUDA events (slowest "
+                                     "rank); context, not the peak"},
         "step_ms_min": min(per_step), "gpu_launches": opt.launches_per_step() * args.steps,
         "clocks": clocks.report(),
     }
